@@ -1,0 +1,385 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 causal forward of path-ordered geometric attention.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c3] [--impl ours|reference]
+
+One step = one forward of PathOrderedGeometricMHA (qkv / edge-MLP / out GEMMs
+in PyTorch, the core region in libhoa) over a batch of synthetic inputs
+already resident in HBM.  Default workload: configs[2] of the baseline
+(B=16, T=4096, d_model=1536, H=16, head_dim=96, bf16 activations, fp32
+rotations, edge_scale 0.05), the configuration the metric is quoted on.
+With N GPUs every rank runs its own batch (batch sharding, no data-path
+collective: weak scaling); rank 0 prints one JSON line.
+
+`--impl reference` times the reference algorithm's CPU implementation (the
+numpy restatement in oracle/, float32, all host threads) on a bounded sample
+of the same workload; under torchrun only rank 0 runs it.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "fwd tokens/s/GPU at T=4096 H=16 d=96 bf16; % roofline; 1/2/4/8-GPU scaling"
+CONFIGS = {
+    # name: (B per GPU, T, d_model, H, dtype)
+    "c2": (64, 512, 192, 4, "bf16"),
+    "c2f32": (64, 512, 192, 4, "fp32"),
+    "c3": (16, 4096, 1536, 16, "bf16"),
+    "c4slice": (16, 2048, 2880, 24, "bf16"),
+}
+EDGE_SCALE = 0.05
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        d["source"] = "measured"
+        return d
+    except Exception:
+        return dict(PEAKS_FALLBACK)
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: str):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", self.gpu, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [s.strip() for s in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        pw = [float(r[3]) for r in rows if r[3].replace(".", "").isdigit()]
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "power_w_max": max(pw) if pw else None, "samples": len(rows), "reasons": reasons}
+
+
+def physical_gpu_index(local_rank: int) -> str:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [s.strip() for s in vis.split(",") if s.strip()]
+        if local_rank < len(ids):
+            return ids[local_rank]
+    return str(local_rank)
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference algorithm's CPU implementation (numpy port)
+# ---------------------------------------------------------------------------
+def cpu_sample_forward(sd_np, D, H, T_sample):
+    import numpy as np
+    from oracle import holonomy_oracle as O
+    rng = np.random.default_rng(0)
+    x = O.round_bf16(rng.standard_normal((1, T_sample, D)).astype(np.float32))
+    t0 = time.perf_counter()
+    O.forward(sd_np, x, H, EDGE_SCALE, np.float32)
+    return time.perf_counter() - t0
+
+
+def cpu_threads():
+    try:
+        from threadpoolctl import threadpool_info
+        n = [i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"]
+        return max(n) if n else 1
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def seeded_params_np(D, H, seed=0):
+    """Weights for the CPU sample: seeded default init, bf16-rounded (the bf16 workload's values)."""
+    import numpy as np
+    import torch
+    from oracle.seeded import seeded_state_dict
+    from oracle.holonomy_oracle import Params
+    sd = seeded_state_dict(D, H, seed)
+    sd = {k: v.to(torch.bfloat16).float() for k, v in sd.items() if not k.startswith(("gq", "gk"))}
+    return Params.from_state_dict(sd, dtype=np.float32)
+
+
+def cpu_sample_len(T):
+    return min(T, 256)
+
+
+def run_reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    B, T, D, H, dt = CONFIGS[args.config]
+    Ts = cpu_sample_len(T)
+    p = seeded_params_np(D, H)
+    times = []
+    for i in range(args.warmup + args.steps):
+        s = cpu_sample_forward(p, D, H, Ts)
+        if i >= args.warmup:
+            times.append(s)
+    sec = statistics.mean(times)
+    val = Ts / sec
+    cores = cpu_threads()
+    line = {
+        "impl": "reference", "metric": METRIC, "value": val, "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": config_obj(args.config, args.gpus),
+        "cpu_baseline": {"value": val, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"1 sequence of T={Ts} at d_model={D}, H={H} per step "
+                                   "(numpy float32 restatement of the reference forward, "
+                                   "bf16-valued inputs/weights)"},
+        "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def config_obj(name, n):
+    B, T, D, H, dt = CONFIGS[name]
+    return {"workload": f"{name}: B={B}/GPU, T={T}, d_model={D}, H={H}, head_dim={D // H}, {dt} "
+                        f"activations, fp32 rotations, edge_scale {EDGE_SCALE}",
+            "global_batch": B * n, "seq_len": T, "d_model": D, "heads": H, "head_dim": D // H,
+            "parallelism": f"batch-sharded x{n} (no collective)",
+            "l2": "inputs and workspace (tens of GB) far exceed the 126 MB L2"}
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def run_ours(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
+
+    from holonomyawareattention_b200 import PathOrderedGeometricMHA, ops
+
+    B, T, D, H, dtn = CONFIGS[args.config]
+    dtype = torch.bfloat16 if dtn == "bf16" else torch.float32
+    d = D // H
+    m_dim = d * (d - 1) // 2
+    torch.manual_seed(0)
+    with torch.device(dev):
+        mod = PathOrderedGeometricMHA(D, n_heads=H, edge_scale=EDGE_SCALE)
+    mod = mod.to(dtype).eval()
+    if args.generator_precision:
+        mod.generator_precision = args.generator_precision
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    x = torch.randn(B, T, D, device=dev, generator=g).to(dtype)
+    mask = torch.tril(torch.ones(T, T, dtype=torch.bool, device=dev))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    stream = torch.cuda.current_stream(dev)
+    clocks = ClockSampler(physical_gpu_index(local))
+    with torch.inference_mode():
+        for _ in range(args.warmup):
+            mod(x, attn_mask=mask)
+        torch.cuda.synchronize(dev)
+        barrier()
+        torch.cuda.synchronize(dev)
+        clocks.start()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            y, _ = mod(x, attn_mask=mask)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        clk = clocks.stop()
+        barrier()
+        ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+        del y
+        value = world * B * T / (ms / 1e3)
+
+        # ---- core region and per-kernel timing (events on the launching stream)
+        qkv = mod.qkv(x).contiguous()
+        a_all = mod.edge_generators(x)
+        chunk = ops.plan_chunk(B, H, T, d, dev)
+        torch.cuda.empty_cache()
+        stage_ms = {"link_local": [], "carry_scan": [], "carry_apply": [], "attn_fwd": []}
+        core_ms = []
+        for it in range(args.warmup + args.steps):
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+            ev[0].record(stream)
+            R, U, M = ops.link_local(a_all, qkv, H, EDGE_SCALE, chunk)
+            ev[1].record(stream)
+            C, _ = ops.carry_scan(M)
+            ev[2].record(stream)
+            qh, kh, vh = ops.carry_apply(U, C, chunk, dtype)
+            ev[3].record(stream)
+            out = ops.attn_fwd(qh, kh, vh, R, C, chunk, B, H, mod.scale, dtype)
+            ev[4].record(stream)
+            torch.cuda.synchronize(dev)
+            if it >= args.warmup:
+                for i, k in enumerate(stage_ms):
+                    stage_ms[k].append(ev[i].elapsed_time(ev[i + 1]))
+                core_ms.append(ev[0].elapsed_time(ev[4]))
+            del R, U, M, C, qh, kh, vh, out
+        stage = {k: statistics.mean(v) for k, v in stage_ms.items()}
+        core = statistics.mean(core_ms)
+        del qkv, a_all
+        torch.cuda.empty_cache()
+
+        # ---- end to end through the public API with host buffers
+        xh = x.cpu().pin_memory()
+        yh = torch.empty(B, T, D, dtype=dtype).pin_memory()
+        xd = torch.empty_like(x)
+        for _ in range(2):
+            xd.copy_(xh, non_blocking=True)
+            yy, _ = mod(xd, attn_mask=mask)
+            yh.copy_(yy, non_blocking=True)
+        torch.cuda.synchronize(dev)
+        barrier()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for _ in range(args.steps):
+            xd.copy_(xh, non_blocking=True)
+            yy, _ = mod(xd, attn_mask=mask)
+            yh.copy_(yy, non_blocking=True)
+        f1.record(stream)
+        torch.cuda.synchronize(dev)
+        e2e_ms = max_over_ranks(f0.elapsed_time(f1) / args.steps)
+        nbytes = x.numel() * x.element_size()
+
+    # ---- roofline of the dominant kernel (link_local) and the BASELINE formula
+    peaks = load_peaks()
+    s_x = 2 if dtype == torch.bfloat16 else 4
+    n_pos = B * H * T
+    link_bytes = n_pos * (m_dim * 4 + 3 * d * s_x)                 # a_all fp32 + q,k,v
+    core_bytes = n_pos * (m_dim * 4 + 4 * d * s_x)                 # + o
+    f_attn = 4.0 * B * H * d * T * (T + 1) / 2
+    f_rot = n_pos * 4 * 2.0 * d ** 3
+    link_s = stage["link_local"] / 1e3
+    hbm = peaks["hbm_gbs"]
+    bf16_peak = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
+    baseline_roof_s = max(f_attn / (bf16_peak * 1e12), core_bytes / (hbm * 1e9))
+    sm_mhz = clk.get("sm_mhz") or 1965.0
+    ffma_peak = 148 * 128 * 2 * sm_mhz * 1e6 / 1e12
+    roofline = {"bound": "hbm", "kernel": "link_local (kernels 1+2)",
+                "achieved": link_bytes / link_s / 1e9, "peak": hbm, "unit": "GB/s",
+                "frac": link_bytes / link_s / 1e9 / hbm, "traffic": args.traffic,
+                "peak_source": f"{peaks['source']} hbm_gbs (of {peaks['source']})",
+                "algorithmic_bytes_per_launch": link_bytes}
+    extra = {
+        "core_ms_per_step": core, "stage_ms": stage, "chunk": chunk,
+        "roofline_baseline_formula": {
+            "definition": "max(F_attn / bf16 peak, (a_all fp32 + q,k,v,o) bytes / HBM BW) over the core region",
+            "target_ms": baseline_roof_s * 1e3, "core_ms": core, "frac": baseline_roof_s * 1e3 / core},
+        "roofline_fp32_rotations": {
+            "definition": "F_rot = N_pos * 4 * 2 d^3 (3 expm products + 1 composition) / link_local time, "
+                          "vs FFMA peak 148 SM x 128 lanes x 2 x median SM clock (nominal, not measured)",
+            "achieved_tflops": f_rot / link_s / 1e12, "peak_tflops": ffma_peak,
+            "frac": f_rot / link_s / 1e12 / ffma_peak},
+    }
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        p = seeded_params_np(D, H)
+        Ts = cpu_sample_len(T)
+        cpu_sample_forward(p, D, H, min(Ts, 32))
+        sec = cpu_sample_forward(p, D, H, Ts)
+        cpu = {"value": Ts / sec, "unit": "tokens/s", "cores": cpu_threads(), "kind": "port",
+               "sample": f"1 sequence of T={Ts} at d_model={D}, H={H} (numpy float32 restatement "
+                         "of the reference forward, bf16-valued inputs/weights)"}
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16" if dtype == torch.bfloat16 else "f32",
+        "data": "synthetic (x ~ N(0,1), seeded default-init weights)",
+        "config": config_obj(args.config, world),
+        "per_gpu_tokens_s": value / world,
+        "roofline": roofline, "cpu_baseline": cpu,
+        "e2e": {"value": world * B * T / (e2e_ms / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes},
+        "gpu_launches": 4 * args.steps, "clocks": clk,
+        "generator_precision": mod.generator_precision,
+        **extra,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", default="c3", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--generator-precision", default=None, choices=[None, "split", "bf16"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--traffic", type=float, default=None,
+                    help="ncu dram bytes per link_local launch, from a capture (scaled), if known")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference_arm(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,158 @@
+"""Drop-in PathOrderedGeometricMHA backed by the sm_100a kernels of libhoa.so.
+
+Same constructor arguments, attributes, submodules (in the same creation
+order, so seeded default init and state_dict keys match) and forward
+signature as the reference module (core/attention.py:27-74,
+core/attention_fast_chunked.py:37-60, 98).  The reference's experiments pick
+the module by import path (`--attn-module`, experiments/session_cherry.py:278,
+445), so `--attn-module holonomyawareattention_b200` selects this one.
+
+Supported inputs are exactly those of the reference's kernel drop-in
+(kernel/attention_kernel.py:193-208): mode "causal", attn_mask exactly
+tril(L), dropout inactive, CUDA input, return_geometry False.  Anything else
+raises NotImplementedError: there is no CPU or PyTorch fallback.
+
+Forward only.  The projections (qkv, edge_mlp, out) run as PyTorch GEMMs;
+everything between them — link rotations, prefix composition, transport,
+causal attention and the inverse transport — runs in libhoa.
+"""
+from __future__ import annotations
+
+import math
+from typing import Dict, Optional, Tuple
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from . import ops
+
+
+def _is_exact_tril(mask: Optional[torch.Tensor], L: int) -> bool:
+    """Same rule as kernel/attention_kernel.py:193-199."""
+    if mask is None or tuple(mask.shape) != (L, L):
+        return False
+    tril = torch.ones(L, L, dtype=torch.bool, device=mask.device).tril()
+    return bool(torch.equal(mask.bool(), tril))
+
+
+class PathOrderedGeometricMHA(nn.Module):
+    """Path-ordered geometric multi-head attention (causal forward on B200).
+
+    Attributes mirror the reference: h, d, m_dim, edge_scale, scale, mode,
+    link_mode, qkv, out, dropout, gqproj, gkproj, edge_mlp.
+
+    ``generator_precision`` (not in the reference) controls how the edge
+    generators are produced when the module runs in bfloat16:
+      * "split" (default): the edge-MLP hidden layer is kept in fp32 and the
+        second GEMM runs as two bf16 GEMMs (high and low halves of the hidden
+        activations) with fp32 output, so the generators carry ~16 bits and
+        long rotation products do not drift;
+      * "bf16": one bf16 GEMM with fp32 output (hidden activations rounded to
+        bf16); about 1e-3 relative error per generator entry, which grows as
+        sqrt(T) along the path product.
+    In float32 the edge MLP runs in fp32, exactly as the reference.
+    """
+
+    def __init__(self, d_model: int, n_heads: int = 4, dropout: float = 0.0,
+                 edge_scale: float = 0.1, mode: str = "causal"):
+        super().__init__()
+        if d_model % n_heads != 0:
+            raise ValueError("d_model must be divisible by n_heads")
+        if mode not in ("causal", "inert"):
+            raise ValueError("mode must be 'causal' or 'inert'")
+        self.h = n_heads
+        self.d = d_model // n_heads
+        self.m_dim = self.d * (self.d - 1) // 2
+        self.edge_scale = edge_scale
+        self.scale = 1.0 / math.sqrt(self.d)
+        self.mode = mode
+
+        # creation order matches core/attention_fast_chunked.py:51-59
+        self.qkv = nn.Linear(d_model, 3 * d_model, bias=False)
+        self.out = nn.Linear(d_model, d_model, bias=False)
+        self.dropout = nn.Dropout(dropout)
+        self.gqproj = nn.Linear(d_model, self.m_dim * n_heads, bias=False)
+        self.gkproj = nn.Linear(d_model, self.m_dim * n_heads, bias=False)
+        self.edge_mlp = nn.Sequential(
+            nn.Linear(2 * d_model, 4 * d_model), nn.GELU(),
+            nn.Linear(4 * d_model, self.m_dim * n_heads),
+        )
+        self.link_mode = "interaction"
+        self.generator_precision = "split"
+        self.chunk: Optional[int] = None          # None: hoa_plan_chunk decides
+        self._tril_ok: Dict[Tuple, bool] = {}
+
+    # ------------------------------------------------------------------
+    def _check_supported(self, x: torch.Tensor, attn_mask, return_geometry: bool) -> None:
+        why = None
+        if self.mode != "causal":
+            why = "mode must be 'causal'"
+        elif self.link_mode != "interaction":
+            why = "link_mode must be 'interaction'"
+        elif return_geometry:
+            why = "return_geometry=True is not supported"
+        elif not x.is_cuda:
+            why = "input must be a CUDA tensor"
+        elif self.training and self.dropout.p != 0.0:
+            why = "dropout must be 0 or the module in eval mode"
+        elif x.dim() != 3 or x.shape[-1] != self.h * self.d:
+            why = f"x must be (B, L, {self.h * self.d})"
+        elif torch.is_grad_enabled() and (x.requires_grad or any(p.requires_grad for p in self.parameters())):
+            why = "forward-only kernels: call under torch.no_grad() / torch.inference_mode()"
+        if why is None and not self._mask_is_tril(attn_mask, x.shape[1]):
+            why = "attn_mask must be exactly tril(L)"
+        if why is not None:
+            raise NotImplementedError(f"PathOrderedGeometricMHA (B200): {why}")
+
+    def _mask_is_tril(self, mask, L: int) -> bool:
+        if mask is None:
+            return False
+        key = (mask.data_ptr(), tuple(mask.shape), mask.dtype, mask._version, str(mask.device))
+        ok = self._tril_ok.get(key)
+        if ok is None:
+            ok = _is_exact_tril(mask, L)
+            if len(self._tril_ok) > 64:
+                self._tril_ok.clear()
+            self._tril_ok[key] = ok
+        return ok
+
+    def edge_generators(self, x: torch.Tensor) -> torch.Tensor:
+        """a_all (B, L, H*m) in fp32, unscaled: edge_mlp([x_t, x_{t+1 mod L}]).
+
+        core/attention_fast_chunked.py:73-76 (the edge_scale multiply happens in
+        the link kernel).
+        """
+        B, L, D = x.shape
+        pair = torch.cat([x, torch.roll(x, shifts=-1, dims=1)], dim=-1)
+        lin0, lin2 = self.edge_mlp[0], self.edge_mlp[2]
+        if x.dtype == torch.float32:
+            return self.edge_mlp(pair)
+        if x.dtype != torch.bfloat16:
+            raise NotImplementedError(f"dtype {x.dtype} is not supported (float32 or bfloat16)")
+        p2 = pair.reshape(B * L, 2 * D)
+        h = torch.mm(p2, lin0.weight.t(), out_dtype=torch.float32)
+        h = F.gelu(h.add_(lin0.bias.float()))
+        w2t = lin2.weight.t()
+        hi = h.to(torch.bfloat16)
+        a = torch.mm(hi, w2t, out_dtype=torch.float32)
+        if self.generator_precision == "split":
+            lo = h.sub_(hi.float()).to(torch.bfloat16)
+            a.add_(torch.mm(lo, w2t, out_dtype=torch.float32))
+        elif self.generator_precision != "bf16":
+            raise ValueError("generator_precision must be 'split' or 'bf16'")
+        a.add_(lin2.bias.float())
+        return a.view(B, L, self.h * self.m_dim)
+
+    def forward(self, x: torch.Tensor, attn_mask: Optional[torch.Tensor] = None,
+                return_geometry: bool = False):
+        self._check_supported(x, attn_mask, return_geometry)
+        B, L, D = x.shape
+        qkv = self.qkv(x)
+        if not qkv.is_contiguous():
+            qkv = qkv.contiguous()
+        a_all = self.edge_generators(x)
+        heads = ops.core_forward(a_all, qkv, self.h, self.edge_scale, self.scale,
+                                 out_dtype=x.dtype, hat_dtype=x.dtype, chunk=self.chunk)
+        y = self.out(heads)
+        return y, None

@@ -1,0 +1,241 @@
+// Kernels (3) and (4): causal online-softmax attention over the transported
+// q^, k^, v^ and the inverse transport out_t = P_t o_t with P_t = R_t C_{t/chunk}.
+//
+// Reference semantics (SiddhiMali/HolonomyAwareAttention):
+//   scores q^_i . k^_j * scale, tril mask with finfo.min, online softmax,
+//   o / l.clamp_min(1e-20), out_i = P_i o_i     core/attention_fast_chunked.py:119-171
+//
+// This file holds the fp32 (SIMT) variant: q^/k^/v^ in fp32 or bf16, every
+// product and the softmax in fp32.  One CTA per (query tile of 64, chain).
+#include "hoa_common.cuh"
+
+namespace hoa {
+
+constexpr int kBQ = 64, kBK = 64, kAttnThreads = 256;
+constexpr int kLDT = kBQ + 4;   // row stride of the transposed tiles (keeps float4 alignment)
+
+template <int DA> struct AttnCfg {
+  static constexpr int CPT = DA / 16;    // output columns per thread
+  static constexpr size_t kQt = (size_t)DA * kLDT, kKt = (size_t)DA * kLDT, kVs = (size_t)kBK * DA,
+                          kPt = (size_t)kBK * kLDT;
+  static constexpr size_t kSmem = (kQt + kKt + kVs + kPt) * sizeof(float);
+};
+
+struct AttnArgs {
+  const void* qh; const void* kh; const void* vh; int hat_dtype;
+  const float* R; const float* C; int chunk, K;
+  void* out; int out_dtype; float scale;
+  int B, H, T, d;
+};
+
+template <int N>
+HOA_DEVICE void lds4(const float* __restrict__ p, float (&v)[N]) {
+  if constexpr (N % 4 == 0) {
+#pragma unroll
+    for (int i = 0; i < N / 4; ++i) {
+      float4 t = reinterpret_cast<const float4*>(p)[i];
+      v[4 * i] = t.x; v[4 * i + 1] = t.y; v[4 * i + 2] = t.z; v[4 * i + 3] = t.w;
+    }
+  } else if constexpr (N % 2 == 0) {
+#pragma unroll
+    for (int i = 0; i < N / 2; ++i) {
+      float2 t = reinterpret_cast<const float2*>(p)[i];
+      v[2 * i] = t.x; v[2 * i + 1] = t.y;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < N; ++i) v[i] = p[i];
+  }
+}
+
+HOA_DEVICE float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+template <int DA>
+__global__ void __launch_bounds__(kAttnThreads) attn_fwd_simt_kernel(AttnArgs p) {
+  using Cf = AttnCfg<DA>;
+  constexpr int CPT = Cf::CPT;
+  extern __shared__ __align__(16) float smem[];
+  float* Qt = smem;                 // [DA][kLDT]   q^ transposed
+  float* Kt = Qt + Cf::kQt;         // [DA][kLDT]   k^ transposed
+  float* Vs = Kt + Cf::kKt;         // [kBK][DA]    v^ row-major
+  float* Pt = Vs + Cf::kVs;         // [kBK][kLDT]  probabilities transposed
+
+  const int tid = threadIdx.x;
+  const int ty = tid / 16, tx = tid % 16;
+  const int r0 = ty * 4, c0 = tx * 4;
+  const int chain = blockIdx.y;
+  const int b = chain / p.H, h = chain % p.H;
+  const int qtile = gridDim.x - 1 - blockIdx.x;     // heaviest causal tiles first
+  const int q0 = qtile * kBQ;
+  const int d = p.d, T = p.T;
+  const long long base = (long long)chain * T * d;
+
+  for (int i = tid; i < kBQ * DA; i += kAttnThreads) {
+    const int r = i / DA, e = i % DA;
+    const int t = q0 + r;
+    Qt[e * kLDT + r] = (t < T && e < d) ? load_elem(p.qh, base + (long long)t * d + e, p.hat_dtype)
+                                        : 0.f;
+  }
+
+  float mrow[4], lrow[4], o[4][CPT];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    mrow[i] = -INFINITY;
+    lrow[i] = 0.f;
+#pragma unroll
+    for (int j = 0; j < CPT; ++j) o[i][j] = 0.f;
+  }
+
+  for (int kt = 0; kt <= qtile; ++kt) {
+    const int k0 = kt * kBK;
+    __syncthreads();
+    for (int i = tid; i < kBK * DA; i += kAttnThreads) {
+      const int r = i / DA, e = i % DA;
+      const int t = k0 + r;
+      const bool ok = t < T && e < d;
+      const long long off = base + (long long)t * d + e;
+      Kt[e * kLDT + r] = ok ? load_elem(p.kh, off, p.hat_dtype) : 0.f;
+      Vs[r * DA + e] = ok ? load_elem(p.vh, off, p.hat_dtype) : 0.f;
+    }
+    __syncthreads();
+
+    float s[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) s[i][j] = 0.f;
+#pragma unroll 4
+    for (int e = 0; e < DA; ++e) {
+      float qa[4], kb[4];
+      lds4<4>(Qt + e * kLDT + r0, qa);
+      lds4<4>(Kt + e * kLDT + c0, kb);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) s[i][j] = fmaf(qa[i], kb[j], s[i][j]);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int qi = q0 + r0 + i;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int kj = k0 + c0 + j;
+        s[i][j] = (kj <= qi && kj < T) ? s[i][j] * p.scale : -INFINITY;
+        mx = fmaxf(mx, s[i][j]);
+      }
+#pragma unroll
+      for (int off = 8; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      const float mnew = fmaxf(mrow[i], mx);
+      const float mref = mnew == -INFINITY ? 0.f : mnew;
+      const float corr = expf(mrow[i] - mref);
+      float rs = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float pv = expf(s[i][j] - mref);
+        s[i][j] = pv;
+        rs += pv;
+      }
+#pragma unroll
+      for (int off = 8; off > 0; off >>= 1) rs += __shfl_xor_sync(0xffffffffu, rs, off);
+      lrow[i] = lrow[i] * corr + rs;
+      mrow[i] = mnew;
+#pragma unroll
+      for (int j = 0; j < CPT; ++j) o[i][j] *= corr;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) Pt[(c0 + j) * kLDT + r0 + i] = s[i][j];
+    }
+    __syncthreads();
+#pragma unroll 4
+    for (int j = 0; j < kBK; ++j) {
+      float pa[4], vb[CPT];
+      lds4<4>(Pt + j * kLDT + r0, pa);
+      lds4<CPT>(Vs + j * DA + tx * CPT, vb);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int jj = 0; jj < CPT; ++jj) o[i][jj] = fmaf(pa[i], vb[jj], o[i][jj]);
+    }
+  }
+
+  // ---- epilogue: o / l, then out_t = R_t (C_k o_t) --------------------------
+  __syncthreads();
+  float* Os = Kt;                   // [kBQ][DA]
+  float* Wv = Qt;                   // [8 warps][DA]
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float inv = 1.f / fmaxf(lrow[i], 1e-20f);
+#pragma unroll
+    for (int j = 0; j < CPT; ++j) Os[(r0 + i) * DA + tx * CPT + j] = o[i][j] * inv;
+  }
+  __syncthreads();
+  const int warp = tid / 32, lane = tid % 32;
+  float* wv = Wv + warp * DA;
+  for (int rr = warp; rr < kBQ; rr += kAttnThreads / 32) {
+    const int t = q0 + rr;
+    if (t >= T) break;
+    const float* orow = Os + rr * DA;
+    const float* Cg = p.C + ((long long)chain * p.K + t / p.chunk) * d * d;
+    const float* Rg = p.R + ((long long)chain * T + t) * d * d;
+    for (int e = 0; e < d; ++e) {
+      float part = 0.f;
+      for (int f = lane; f < d; f += 32) part = fmaf(Cg[e * d + f], orow[f], part);
+      part = warp_sum(part);
+      if (lane == 0) wv[e] = part;
+    }
+    __syncwarp();
+    const long long obase = (((long long)b * T + t) * p.H + h) * d;
+    for (int e = 0; e < d; ++e) {
+      float part = 0.f;
+      for (int f = lane; f < d; f += 32) part = fmaf(Rg[e * d + f], wv[f], part);
+      part = warp_sum(part);
+      if (lane == 0) store_elem(p.out, obase + e, p.out_dtype, part);
+    }
+    __syncwarp();
+  }
+}
+
+template <int DA>
+int launch_attn(const AttnArgs& a, cudaStream_t s) {
+  using Cf = AttnCfg<DA>;
+  if (cudaFuncSetAttribute(attn_fwd_simt_kernel<DA>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)Cf::kSmem) != cudaSuccess)
+    return HOA_ERR_LAUNCH;
+  dim3 grid((unsigned)ceil_div(a.T, kBQ), (unsigned)(a.B * a.H));
+  attn_fwd_simt_kernel<DA><<<grid, kAttnThreads, Cf::kSmem, s>>>(a);
+  return launch_status();
+}
+
+}  // namespace hoa
+
+using namespace hoa;
+
+extern "C" int hoa_attn_fwd(const void* qh, const void* kh, const void* vh, int hat_dtype,
+                            const float* R, const float* C, int chunk, void* out, int out_dtype,
+                            float softmax_scale, int B, int H, int T, int d, void* stream) {
+  if (!qh || !kh || !vh || !R || !C || !out || B < 1 || H < 1 || T < 1 || d < 1 || chunk < 1)
+    return HOA_ERR_INVALID_ARG;
+  if ((hat_dtype != HOA_F32 && hat_dtype != HOA_BF16) ||
+      (out_dtype != HOA_F32 && out_dtype != HOA_BF16))
+    return HOA_ERR_UNSUPPORTED;
+  if ((long long)B * H > 65535) return HOA_ERR_UNSUPPORTED;
+  AttnArgs a{qh, kh, vh, hat_dtype, R, C, chunk, ceil_div(T, chunk), out, out_dtype,
+             softmax_scale, B, H, T, d};
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int da = ((d + 15) / 16) * 16;
+  switch (da) {
+    case 16: return launch_attn<16>(a, s);
+    case 32: return launch_attn<32>(a, s);
+    case 48: return launch_attn<48>(a, s);
+    case 64: return launch_attn<64>(a, s);
+    case 80: return launch_attn<80>(a, s);
+    case 96: return launch_attn<96>(a, s);
+    case 112: return launch_attn<112>(a, s);
+    case 128: return launch_attn<128>(a, s);
+    default: return HOA_ERR_UNSUPPORTED;
+  }
+}

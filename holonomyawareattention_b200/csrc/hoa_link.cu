@@ -1,0 +1,580 @@
+// Kernels (1) and (2): link rotations G_t = expm(skew(edge_scale * a_t)) and the
+// ordered prefix composition P_{t+1} = G_t P_t, chunked so that every
+// (chain, chunk) unit runs independently, then joined by a carry scan.
+//
+// Reference semantics (SiddhiMali/HolonomyAwareAttention):
+//   skew_from_vec            core/utils.py:4-27   (row-major strict upper triangle, A[j,i] = -A[i,j])
+//   so_exp = matrix_exp      core/utils.py:30-52
+//   a_all * edge_scale       core/attention_fast_chunked.py:77
+//   prefix loop              core/attention_fast_chunked.py:89-94
+//   transport q^ = P^T q     core/attention_fast_chunked.py:108-110
+//
+// Arithmetic is fp32 throughout (FFMA).  Each unit keeps four d x d matrices
+// in shared memory: the running local product R, the generator A (later G^T),
+// and two operand buffers.  Each thread owns a TM x TN tile of every product.
+#include "hoa_common.cuh"
+
+namespace hoa {
+
+// ---------------------------------------------------------------------------
+// Degree-8 Taylor polynomial of exp(A) in three matrix products
+// (Bader, Blanes & Casas, Mathematics 7 (2019) 1174, the 3-product T8 scheme):
+//   A2 = A^2
+//   A4 = A2 (x1 A + x2 A2)
+//   A8 = (x3 A2 + A4)(x4 I + x5 A + x6 A2 + x7 A4)
+//   T8 = I + A + y2 A2 + A8            == sum_{k=0..8} A^k / k!   (exact identity)
+// Matching the coefficients of A^2..A^8 gives x1 = 4 x2 and, with z = x3/x2,
+// z^2 + 4 z - 704 = 0; we take z = -2 + sqrt(708) (the root with small
+// coefficients) and fix the free scale by x4 = 1:
+//   x2 = (1/6 - 11 z/2520)/4, x1 = 4 x2, x3 = z x2, x5 = 11/(2520 x2),
+//   x6 = (1/1008 - z/40320)/x2, x7 = 1/(40320 x2^2), y2 = 1/2 - x3 x4.
+// (Values below evaluated in double precision from those formulas.)
+// ---------------------------------------------------------------------------
+__constant__ float kT8[8] = {
+    0.059249617736388274f,  // x1
+    0.014812404434097069f,  // x2
+    0.36450763864714936f,   // x3
+    1.0f,                   // x4
+    0.29469080354241967f,   // x5
+    0.025771599210148963f,  // x6
+    0.11303901220301756f,   // x7
+    0.13549236135285064f,   // y2
+};
+
+// Largest theta = sqrt(||A^2||_1) >= ||A||_2 for which the Taylor remainder
+// sum_{k>=9} theta^k/k! stays below 3e-8 (< half an fp32 ulp of 1).  For a
+// skew-symmetric (normal) A the remainder bound holds in the 2-norm, and e^A
+// is orthogonal, so this is a relative bound.  Larger norms are scaled by
+// 2^-s and squared s times.
+constexpr float kTheta8 = 0.6f;
+
+template <int DP> struct LinkTile;
+template <> struct LinkTile<8>   { static constexpr int TM = 2, TN = 2; };
+template <> struct LinkTile<16>  { static constexpr int TM = 2, TN = 2; };
+template <> struct LinkTile<32>  { static constexpr int TM = 4, TN = 4; };
+template <> struct LinkTile<48>  { static constexpr int TM = 6, TN = 6; };
+template <> struct LinkTile<64>  { static constexpr int TM = 8, TN = 8; };
+template <> struct LinkTile<96>  { static constexpr int TM = 6, TN = 6; };
+template <> struct LinkTile<120> { static constexpr int TM = 8, TN = 8; };
+
+template <int DP> struct LinkCfg {
+  static constexpr int TM = LinkTile<DP>::TM, TN = LinkTile<DP>::TN;
+  static constexpr int GX = DP / TN, GY = DP / TM;     // thread grid over the output
+  static constexpr int ACTIVE = GX * GY;
+  static constexpr int NT = ACTIVE <= 32 ? 32 : ((ACTIVE + 31) / 32) * 32;
+  static constexpr int MAT = DP * DP;                   // floats per matrix (row stride DP)
+  static constexpr size_t kLinkSmem = (4 * MAT + 4 * DP) * sizeof(float);
+  static constexpr size_t kScanSmem = (2 * MAT) * sizeof(float);
+};
+
+template <int N>
+HOA_DEVICE void lds_vec(const float* __restrict__ p, float (&v)[N]) {
+  if constexpr (N % 4 == 0) {
+#pragma unroll
+    for (int i = 0; i < N / 4; ++i) {
+      float4 t = reinterpret_cast<const float4*>(p)[i];
+      v[4 * i] = t.x; v[4 * i + 1] = t.y; v[4 * i + 2] = t.z; v[4 * i + 3] = t.w;
+    }
+  } else if constexpr (N % 2 == 0) {
+#pragma unroll
+    for (int i = 0; i < N / 2; ++i) {
+      float2 t = reinterpret_cast<const float2*>(p)[i];
+      v[2 * i] = t.x; v[2 * i + 1] = t.y;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < N; ++i) v[i] = p[i];
+  }
+}
+
+// acc[i][j] += sum_k X[r0+i][k] * Y[k][c0+j], with X supplied column-major
+// (Xt[k][r] = X[r][k]) and Y row-major, both DP x DP with row stride DP.
+template <int DP, int TM, int TN>
+HOA_DEVICE void mm_acc(const float* __restrict__ Xt, const float* __restrict__ Y, int r0, int c0,
+                       float (&acc)[TM][TN]) {
+#pragma unroll 4
+  for (int k = 0; k < DP; ++k) {
+    float xa[TM], yb[TN];
+    lds_vec<TM>(Xt + k * DP + r0, xa);
+    lds_vec<TN>(Y + k * DP + c0, yb);
+#pragma unroll
+    for (int i = 0; i < TM; ++i)
+#pragma unroll
+      for (int j = 0; j < TN; ++j) acc[i][j] = fmaf(xa[i], yb[j], acc[i][j]);
+  }
+}
+
+template <int TM, int TN>
+HOA_DEVICE void zero_acc(float (&acc)[TM][TN]) {
+#pragma unroll
+  for (int i = 0; i < TM; ++i)
+#pragma unroll
+    for (int j = 0; j < TN; ++j) acc[i][j] = 0.f;
+}
+
+// Row of the strict-upper-triangle entry idx: largest i with S_i <= idx,
+// S_i = i (2d - i - 1) / 2 (row-major order of core/utils.py:20-26).
+HOA_DEVICE int triu_row(int idx, int d) {
+  const float b = 2.f * d - 1.f;
+  int i = (int)floorf((b - sqrtf(fmaxf(b * b - 8.f * idx, 0.f))) * 0.5f);
+  i = max(0, min(i, d - 2));
+  while (i + 1 <= d - 2 && (i + 1) * (2 * d - i - 2) / 2 <= idx) ++i;
+  while (i > 0 && i * (2 * d - i - 1) / 2 > idx) --i;
+  return i;
+}
+
+struct LinkArgs {
+  const void* a; int a_dtype; float edge_scale;
+  const void* qkv; int qkv_dtype;
+  float* R; float* U; float* M;
+  int B, H, T, d, chunk, K;
+};
+
+// One CTA per (chain, chunk).  For every position t of the chunk it writes
+// R_t and U_t = R_t^T [q_t, k_t, v_t], then folds edge t into R.
+template <int DP>
+__global__ void __launch_bounds__(LinkCfg<DP>::NT, 1) link_local_kernel(LinkArgs p) {
+  using C = LinkCfg<DP>;
+  constexpr int TM = C::TM, TN = C::TN, NT = C::NT;
+  extern __shared__ __align__(16) float smem[];
+  float* bufR = smem;              // running local product R (row-major)
+  float* bufA = bufR + C::MAT;     // A, later G^T
+  float* buf1 = bufA + C::MAT;     // A2, later L^T
+  float* buf2 = buf1 + C::MAT;     // T1 = x1 A + x2 A2, later the right factor of A8
+  float* svec = buf2 + C::MAT;     // q, k, v of the current position (3*DP)
+  float* colsum = svec + 3 * DP;   // column abs-sums of A2 (DP)
+  __shared__ int s_squarings;
+
+  const int tid = threadIdx.x;
+  const int chain = blockIdx.x / p.K;
+  const int kc = blockIdx.x % p.K;
+  const int b = chain / p.H, h = chain % p.H;
+  const int d = p.d;
+  const int m = d * (d - 1) / 2;
+  const int t0 = kc * p.chunk;
+  const int t1 = min(t0 + p.chunk, p.T);
+  const bool active = tid < C::ACTIVE;
+  const int r0 = (tid / C::GX) * TM, c0 = (tid % C::GX) * TN;
+
+  for (int i = tid; i < C::MAT; i += NT) bufR[i] = (i / DP == i % DP) ? 1.f : 0.f;
+  __syncthreads();
+
+  float acc[TM][TN];
+  float E[TM][TN];
+  for (int t = t0; t < t1; ++t) {
+    // ---- position t: R_t and the locally transported q, k, v -------------
+    const long long pos = (long long)chain * p.T + t;
+    float* Rg = p.R + pos * d * d;
+    for (int i = tid; i < d * d; i += NT) Rg[i] = bufR[(i / d) * DP + (i % d)];
+    const long long qbase = (((long long)b * p.T + t) * p.H + h) * 3LL * d;
+    for (int i = tid; i < 3 * DP; i += NT) {
+      const int v = i / DP, e = i % DP;
+      svec[i] = e < d ? load_elem(p.qkv, qbase + (long long)v * d + e, p.qkv_dtype) : 0.f;
+    }
+    // ---- edge t: A = skew(edge_scale * a_t) ------------------------------
+    const long long abase = (((long long)b * p.T + t) * p.H + h) * (long long)m;
+    for (int idx = tid; idx < m; idx += NT) {
+      const int i = triu_row(idx, d);
+      const int j = idx - i * (2 * d - i - 1) / 2 + i + 1;
+      const float v = __fmul_rn(load_elem(p.a, abase + idx, p.a_dtype), p.edge_scale);
+      bufA[i * DP + j] = v;
+      bufA[j * DP + i] = -v;
+    }
+    for (int i = tid; i < DP; i += NT) { bufA[i * DP + i] = 0.f; colsum[i] = 0.f; }
+    if (d < DP) {
+      for (int i = tid; i < DP * (DP - d); i += NT) {
+        const int r = i / (DP - d), c = d + i % (DP - d);
+        bufA[r * DP + c] = 0.f;
+        bufA[c * DP + r] = 0.f;
+      }
+    }
+    __syncthreads();
+    float* Ug = p.U + pos * 3 * d;
+    for (int i = tid; i < 3 * d; i += NT) {
+      const int v = i / d, e = i % d;
+      float s = 0.f;
+      for (int r = 0; r < d; ++r) s = fmaf(bufR[r * DP + e], svec[v * DP + r], s);
+      Ug[i] = s;
+    }
+
+    // ---- A2 = A A = -(A^T A); theta^2 = ||A2||_1 -------------------------
+    zero_acc(acc);
+    if (active) {
+      mm_acc<DP, TM, TN>(bufA, bufA, r0, c0, acc);
+#pragma unroll
+      for (int j = 0; j < TN; ++j) {
+        float cs = 0.f;
+#pragma unroll
+        for (int i = 0; i < TM; ++i) cs += fabsf(acc[i][j]);
+        atomicAdd(&colsum[c0 + j], cs);
+      }
+    }
+    __syncthreads();
+    if (tid < 32) {
+      float mx = 0.f;
+      for (int c = tid; c < DP; c += 32) mx = fmaxf(mx, colsum[c]);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      if (tid == 0) {
+        float theta = sqrtf(mx);
+        int s = 0;
+        while (theta > kTheta8 && s < 64) { theta *= 0.5f; ++s; }
+        s_squarings = s;
+      }
+    }
+    __syncthreads();
+    const int nsq = s_squarings;
+    const float sa = ldexpf(1.f, -nsq), sa2 = ldexpf(1.f, -2 * nsq);
+    const float x1 = kT8[0], x2 = kT8[1], x3 = kT8[2], x4 = kT8[3], x5 = kT8[4], x6 = kT8[5],
+                x7 = kT8[6], y2 = kT8[7];
+
+    if (active) {
+#pragma unroll
+      for (int i = 0; i < TM; ++i)
+#pragma unroll
+        for (int j = 0; j < TN; ++j) {
+          const int o = (r0 + i) * DP + c0 + j;
+          const float a2 = -acc[i][j] * sa2;
+          buf1[o] = a2;
+          buf2[o] = x1 * (bufA[o] * sa) + x2 * a2;
+        }
+    }
+    __syncthreads();
+
+    // ---- A4 = A2 T1 (A2 symmetric, so buf1 serves as its transpose) -------
+    zero_acc(acc);
+    if (active) mm_acc<DP, TM, TN>(buf1, buf2, r0, c0, acc);
+    __syncthreads();
+    if (active) {
+#pragma unroll
+      for (int i = 0; i < TM; ++i)
+#pragma unroll
+        for (int j = 0; j < TN; ++j) {
+          const int r = r0 + i, c = c0 + j, o = r * DP + c;
+          const float a = bufA[o] * sa, a2 = buf1[o], a4 = acc[i][j];
+          const float id = (r == c) ? 1.f : 0.f;
+          buf2[o] = x4 * id + x5 * a + x6 * a2 + x7 * a4;   // right factor
+          E[i][j] = id + a + y2 * a2;                          // I + A + y2 A2
+          acc[i][j] = x3 * a2 + a4;                            // left factor L
+        }
+    }
+    __syncthreads();
+    if (active) {
+#pragma unroll
+      for (int i = 0; i < TM; ++i)
+#pragma unroll
+        for (int j = 0; j < TN; ++j) buf1[(c0 + j) * DP + r0 + i] = acc[i][j];   // L^T
+    }
+    __syncthreads();
+
+    // ---- G = E + L Rf; then s squarings ------------------------------------
+    if (active) {
+#pragma unroll
+      for (int i = 0; i < TM; ++i)
+#pragma unroll
+        for (int j = 0; j < TN; ++j) acc[i][j] = E[i][j];
+      mm_acc<DP, TM, TN>(buf1, buf2, r0, c0, acc);
+#pragma unroll
+      for (int i = 0; i < TM; ++i)
+#pragma unroll
+        for (int j = 0; j < TN; ++j) bufA[(c0 + j) * DP + r0 + i] = acc[i][j];   // G^T
+    }
+    for (int sq = 0; sq < nsq; ++sq) {
+      __syncthreads();
+      if (active) {
+#pragma unroll
+        for (int i = 0; i < TM; ++i)
+#pragma unroll
+          for (int j = 0; j < TN; ++j) buf2[(r0 + i) * DP + c0 + j] = acc[i][j];   // G
+      }
+      __syncthreads();
+      zero_acc(acc);
+      if (active) mm_acc<DP, TM, TN>(bufA, buf2, r0, c0, acc);
+      __syncthreads();
+      if (active) {
+#pragma unroll
+        for (int i = 0; i < TM; ++i)
+#pragma unroll
+          for (int j = 0; j < TN; ++j) bufA[(c0 + j) * DP + r0 + i] = acc[i][j];
+      }
+    }
+    __syncthreads();
+
+    // ---- R <- G R ----------------------------------------------------------
+    zero_acc(acc);
+    if (active) mm_acc<DP, TM, TN>(bufA, bufR, r0, c0, acc);
+    __syncthreads();
+    if (active) {
+#pragma unroll
+      for (int i = 0; i < TM; ++i)
+#pragma unroll
+        for (int j = 0; j < TN; ++j) bufR[(r0 + i) * DP + c0 + j] = acc[i][j];
+    }
+    __syncthreads();
+  }
+  // chunk total: R after the chunk's last edge
+  float* Mg = p.M + ((long long)chain * p.K + kc) * d * d;
+  for (int i = tid; i < d * d; i += NT) Mg[i] = bufR[(i / d) * DP + (i % d)];
+}
+
+// C_0 = carry_in (or I), C_{k+1} = M_k C_k.  One CTA per chain.
+template <int DP>
+__global__ void __launch_bounds__(LinkCfg<DP>::NT, 1)
+carry_scan_kernel(const float* __restrict__ M, const float* __restrict__ carry_in,
+                  float* __restrict__ Cout, float* __restrict__ total_out, int K, int d) {
+  using Cf = LinkCfg<DP>;
+  constexpr int TM = Cf::TM, TN = Cf::TN, NT = Cf::NT;
+  extern __shared__ __align__(16) float smem[];
+  float* bufC = smem;             // current carry (row-major)
+  float* bufX = bufC + Cf::MAT;   // M_k^T
+  const int tid = threadIdx.x;
+  const int chain = blockIdx.x;
+  const bool active = tid < Cf::ACTIVE;
+  const int r0 = (tid / Cf::GX) * TM, c0 = (tid % Cf::GX) * TN;
+
+  for (int i = tid; i < Cf::MAT; i += NT) {
+    const int r = i / DP, c = i % DP;
+    float v = (r == c) ? 1.f : 0.f;
+    if (carry_in != nullptr && r < d && c < d) v = carry_in[(long long)chain * d * d + r * d + c];
+    bufC[i] = v;
+    bufX[i] = (r == c) ? 1.f : 0.f;
+  }
+  __syncthreads();
+  float acc[TM][TN];
+  for (int k = 0; k < K; ++k) {
+    float* Cg = Cout + ((long long)chain * K + k) * d * d;
+    for (int i = tid; i < d * d; i += NT) Cg[i] = bufC[(i / d) * DP + (i % d)];
+    const float* Mg = M + ((long long)chain * K + k) * d * d;
+    for (int i = tid; i < d * d; i += NT) bufX[(i % d) * DP + (i / d)] = Mg[i];
+    __syncthreads();
+    zero_acc(acc);
+    if (active) mm_acc<DP, TM, TN>(bufX, bufC, r0, c0, acc);
+    __syncthreads();
+    if (active) {
+#pragma unroll
+      for (int i = 0; i < TM; ++i)
+#pragma unroll
+        for (int j = 0; j < TN; ++j) bufC[(r0 + i) * DP + c0 + j] = acc[i][j];
+    }
+    __syncthreads();
+  }
+  if (total_out != nullptr) {
+    float* Tg = total_out + (long long)chain * d * d;
+    for (int i = tid; i < d * d; i += NT) Tg[i] = bufC[(i / d) * DP + (i % d)];
+  }
+}
+
+// hat_v[t] = C_k^T U_v[t] for v in {q, k, v}.  One CTA per (chain, chunk).
+constexpr int kApplyThreads = 256;
+constexpr int kApplyPos = 8;   // positions staged per step
+
+__global__ void __launch_bounds__(kApplyThreads)
+carry_apply_kernel(const float* __restrict__ U, const float* __restrict__ Cin, void* qh, void* kh,
+                   void* vh, int hat_dtype, int T, int d, int chunk, int K) {
+  extern __shared__ __align__(16) float smem[];
+  float* Cs = smem;                 // d*d, row-major
+  float* Us = Cs + d * d;           // kApplyPos * 3 * d
+  const int tid = threadIdx.x;
+  const int chain = blockIdx.x / K;
+  const int kc = blockIdx.x % K;
+  const int t0 = kc * chunk, t1 = min(t0 + chunk, T);
+  const float* Cg = Cin + ((long long)chain * K + kc) * d * d;
+  for (int i = tid; i < d * d; i += kApplyThreads) Cs[i] = Cg[i];
+  void* outs[3] = {qh, kh, vh};
+  for (int tb = t0; tb < t1; tb += kApplyPos) {
+    const int np = min(kApplyPos, t1 - tb);
+    __syncthreads();
+    const float* Ug = U + ((long long)chain * T + tb) * 3 * d;
+    for (int i = tid; i < np * 3 * d; i += kApplyThreads) Us[i] = Ug[i];
+    __syncthreads();
+    for (int i = tid; i < np * 3 * d; i += kApplyThreads) {
+      const int e = i % d, v = (i / d) % 3, pp = i / (3 * d);
+      const float* u = Us + (pp * 3 + v) * d;
+      float s = 0.f;
+      for (int r = 0; r < d; ++r) s = fmaf(Cs[r * d + e], u[r], s);
+      store_elem(outs[v], ((long long)chain * T + tb + pp) * d + e, hat_dtype, s);
+    }
+  }
+}
+
+template <int DP>
+int launch_link_local(const LinkArgs& a, cudaStream_t s) {
+  using C = LinkCfg<DP>;
+  if (cudaFuncSetAttribute(link_local_kernel<DP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)C::kLinkSmem) != cudaSuccess)
+    return HOA_ERR_LAUNCH;
+  const long long units = (long long)a.B * a.H * a.K;
+  link_local_kernel<DP><<<(unsigned)units, C::NT, C::kLinkSmem, s>>>(a);
+  return launch_status();
+}
+
+template <int DP>
+int launch_carry_scan(const float* M, const float* cin, float* C, float* tot, int BH, int K, int d,
+                      cudaStream_t s) {
+  using Cf = LinkCfg<DP>;
+  if (cudaFuncSetAttribute(carry_scan_kernel<DP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)Cf::kScanSmem) != cudaSuccess)
+    return HOA_ERR_LAUNCH;
+  carry_scan_kernel<DP><<<BH, Cf::NT, Cf::kScanSmem, s>>>(M, cin, C, tot, K, d);
+  return launch_status();
+}
+
+}  // namespace hoa
+
+using namespace hoa;
+
+static bool valid_dtype(int t) { return t == HOA_F32 || t == HOA_BF16; }
+
+extern "C" int hoa_abi_version(void) { return 1; }
+extern "C" int hoa_max_head_dim(void) { return 120; }
+
+extern "C" const char* hoa_status_string(int st) {
+  switch (st) {
+    case HOA_OK: return "ok";
+    case HOA_ERR_INVALID_ARG: return "invalid argument";
+    case HOA_ERR_UNSUPPORTED: return "unsupported head dimension or dtype";
+    case HOA_ERR_LAUNCH: return "CUDA launch failed";
+    case HOA_ERR_WORKSPACE: return "workspace too small";
+    case HOA_ERR_TIMEOUT: return "device-side wait timed out";
+    default: return "unknown status";
+  }
+}
+
+extern "C" int hoa_plan_chunk(int B, int H, int T, int d, int num_sms) {
+  if (T < 16) return T > 0 ? T : 1;
+  const int dp = padded_dim(d);
+  // resident units per SM, from the shared-memory footprint of the link kernel
+  const size_t smem = (size_t)(4 * dp * dp + 4 * dp) * sizeof(float);
+  int per_sm = smem > 0 ? (int)(228 * 1024 / (smem + 1024)) : 1;
+  per_sm = per_sm < 1 ? 1 : (per_sm > 8 ? 8 : per_sm);
+  const long long chains = (long long)B * H;
+  const long long slots = (long long)(num_sms > 0 ? num_sms : 148) * per_sm;
+  // aim for ~8 waves of units, so that the partial last wave costs little
+  long long want = (8 * slots + chains - 1) / chains;
+  if (want < 1) want = 1;
+  long long chunk = (T + want - 1) / want;
+  chunk = ((chunk + 15) / 16) * 16;
+  if (chunk < 16) chunk = 16;
+  if (chunk > T) chunk = T;
+  return (int)chunk;
+}
+
+extern "C" int hoa_link_local(const void* a_all, int a_dtype, float edge_scale, const void* qkv,
+                              int qkv_dtype, float* R, float* U, float* M, int B, int H, int T,
+                              int d, int chunk, void* stream) {
+  if (!a_all || !qkv || !R || !U || !M || B < 1 || H < 1 || T < 1 || d < 1 || chunk < 1)
+    return HOA_ERR_INVALID_ARG;
+  if (!valid_dtype(a_dtype) || !valid_dtype(qkv_dtype)) return HOA_ERR_UNSUPPORTED;
+  LinkArgs a{a_all, a_dtype, edge_scale, qkv, qkv_dtype, R, U, M, B, H, T, d, chunk,
+             ceil_div(T, chunk)};
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  switch (padded_dim(d)) {
+    case 8: return launch_link_local<8>(a, s);
+    case 16: return launch_link_local<16>(a, s);
+    case 32: return launch_link_local<32>(a, s);
+    case 48: return launch_link_local<48>(a, s);
+    case 64: return launch_link_local<64>(a, s);
+    case 96: return launch_link_local<96>(a, s);
+    case 120: return launch_link_local<120>(a, s);
+    default: return HOA_ERR_UNSUPPORTED;
+  }
+}
+
+extern "C" int hoa_carry_scan(const float* M, const float* carry_in, float* C, float* total_out,
+                              int BH, int K, int d, void* stream) {
+  if (!M || !C || BH < 1 || K < 1 || d < 1) return HOA_ERR_INVALID_ARG;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  switch (padded_dim(d)) {
+    case 8: return launch_carry_scan<8>(M, carry_in, C, total_out, BH, K, d, s);
+    case 16: return launch_carry_scan<16>(M, carry_in, C, total_out, BH, K, d, s);
+    case 32: return launch_carry_scan<32>(M, carry_in, C, total_out, BH, K, d, s);
+    case 48: return launch_carry_scan<48>(M, carry_in, C, total_out, BH, K, d, s);
+    case 64: return launch_carry_scan<64>(M, carry_in, C, total_out, BH, K, d, s);
+    case 96: return launch_carry_scan<96>(M, carry_in, C, total_out, BH, K, d, s);
+    case 120: return launch_carry_scan<120>(M, carry_in, C, total_out, BH, K, d, s);
+    default: return HOA_ERR_UNSUPPORTED;
+  }
+}
+
+extern "C" int hoa_carry_apply(const float* U, const float* C, void* qh, void* kh, void* vh,
+                               int hat_dtype, int BH, int T, int d, int chunk, void* stream) {
+  if (!U || !C || !qh || !kh || !vh || BH < 1 || T < 1 || d < 1 || chunk < 1)
+    return HOA_ERR_INVALID_ARG;
+  if (!valid_dtype(hat_dtype)) return HOA_ERR_UNSUPPORTED;
+  if (padded_dim(d) == 0) return HOA_ERR_UNSUPPORTED;
+  const int K = ceil_div(T, chunk);
+  const size_t smem = (size_t)(d * d + kApplyPos * 3 * d) * sizeof(float);
+  if (cudaFuncSetAttribute(carry_apply_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem) != cudaSuccess)
+    return HOA_ERR_LAUNCH;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  carry_apply_kernel<<<(unsigned)((long long)BH * K), kApplyThreads, smem, s>>>(
+      U, C, qh, kh, vh, hat_dtype, T, d, chunk, K);
+  return launch_status();
+}
+
+// ---------------------------------------------------------------------------
+// whole core region
+// ---------------------------------------------------------------------------
+namespace {
+struct CoreLayout {
+  size_t R, U, M, C, qh, kh, vh, total;
+};
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+CoreLayout core_layout(int B, int H, int T, int d, int chunk, int hat_dtype) {
+  const size_t BH = (size_t)B * H;
+  const size_t K = (size_t)((T + chunk - 1) / chunk);
+  const size_t hs = hat_dtype == HOA_BF16 ? 2 : 4;
+  CoreLayout L{};
+  size_t off = 0;
+  L.R = off; off = align256(off + BH * T * d * d * sizeof(float));
+  L.U = off; off = align256(off + BH * T * 3 * d * sizeof(float));
+  L.M = off; off = align256(off + BH * K * d * d * sizeof(float));
+  L.C = off; off = align256(off + BH * K * d * d * sizeof(float));
+  L.qh = off; off = align256(off + BH * T * d * hs);
+  L.kh = off; off = align256(off + BH * T * d * hs);
+  L.vh = off; off = align256(off + BH * T * d * hs);
+  L.total = off;
+  return L;
+}
+}  // namespace
+
+extern "C" size_t hoa_core_workspace_bytes(int B, int H, int T, int d, int chunk, int hat_dtype) {
+  if (B < 1 || H < 1 || T < 1 || d < 1 || chunk < 1) return 0;
+  return core_layout(B, H, T, d, chunk, hat_dtype).total;
+}
+
+extern "C" int hoa_core_forward(const void* a_all, int a_dtype, float edge_scale, const void* qkv,
+                                int qkv_dtype, void* out, int out_dtype, int hat_dtype,
+                                float softmax_scale, const float* carry_in, float* total_out,
+                                int B, int H, int T, int d, int chunk, void* workspace,
+                                size_t workspace_bytes, void* stream) {
+  if (!a_all || !qkv || !out || !workspace || B < 1 || H < 1 || T < 1 || d < 1 || chunk < 1)
+    return HOA_ERR_INVALID_ARG;
+  if (!valid_dtype(a_dtype) || !valid_dtype(qkv_dtype) || !valid_dtype(out_dtype) ||
+      !valid_dtype(hat_dtype))
+    return HOA_ERR_UNSUPPORTED;
+  if (padded_dim(d) == 0) return HOA_ERR_UNSUPPORTED;
+  const CoreLayout L = core_layout(B, H, T, d, chunk, hat_dtype);
+  if (workspace_bytes < L.total) return HOA_ERR_WORKSPACE;
+  char* w = static_cast<char*>(workspace);
+  float* R = reinterpret_cast<float*>(w + L.R);
+  float* U = reinterpret_cast<float*>(w + L.U);
+  float* M = reinterpret_cast<float*>(w + L.M);
+  float* C = reinterpret_cast<float*>(w + L.C);
+  void* qh = w + L.qh;
+  void* kh = w + L.kh;
+  void* vh = w + L.vh;
+  const int K = ceil_div(T, chunk);
+  int st = hoa_link_local(a_all, a_dtype, edge_scale, qkv, qkv_dtype, R, U, M, B, H, T, d, chunk,
+                          stream);
+  if (st != HOA_OK) return st;
+  st = hoa_carry_scan(M, carry_in, C, total_out, B * H, K, d, stream);
+  if (st != HOA_OK) return st;
+  st = hoa_carry_apply(U, C, qh, kh, vh, hat_dtype, B * H, T, d, chunk, stream);
+  if (st != HOA_OK) return st;
+  return hoa_attn_fwd(qh, kh, vh, hat_dtype, R, C, chunk, out, out_dtype, softmax_scale, B, H, T,
+                      d, stream);
+}

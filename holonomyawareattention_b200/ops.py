@@ -1,0 +1,150 @@
+"""Tensor-level wrappers over the libhoa C ABI (include/hoa.h).
+
+Each function validates shapes/dtypes/devices, allocates outputs and scratch
+with PyTorch (the C ABI never allocates), and enqueues the kernels on the
+current CUDA stream.  There is no fallback path: a missing library, a CPU
+tensor or an unsupported shape raises.
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional, Tuple
+
+import torch
+
+from . import _lib
+
+_DT = {torch.float32: _lib.HOA_F32, torch.bfloat16: _lib.HOA_BF16}
+
+
+def _dtype_code(t: torch.dtype) -> int:
+    try:
+        return _DT[t]
+    except KeyError:
+        raise NotImplementedError(f"dtype {t} is not supported (float32 or bfloat16)") from None
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return None if t is None else t.data_ptr()
+
+
+def _stream(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _need_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise NotImplementedError("the B200 kernels need CUDA tensors (there is no CPU path)")
+
+
+def _contig(t: torch.Tensor, name: str) -> torch.Tensor:
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    return t
+
+
+def plan_chunk(B: int, H: int, T: int, d: int, device=None) -> int:
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    return int(_lib.load().hoa_plan_chunk(B, H, T, d, sms))
+
+
+def core_forward(a_all: torch.Tensor, qkv: torch.Tensor, n_heads: int, edge_scale: float,
+                 softmax_scale: Optional[float] = None, out_dtype: Optional[torch.dtype] = None,
+                 hat_dtype: Optional[torch.dtype] = None, chunk: Optional[int] = None,
+                 carry_in: Optional[torch.Tensor] = None,
+                 total_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Core region (kernels 1-4): a_all (B,T,H*m) and qkv (B,T,3D) -> heads (B,T,D).
+
+    ``a_all`` is the raw edge-MLP output (edge_scale is applied in the kernel,
+    as core/attention_fast_chunked.py:77 does).  ``carry_in`` / ``total_out``
+    are optional (B*H, d, d) fp32 tensors (see hoa_core_forward).
+    """
+    _need_cuda(a_all, qkv, carry_in, total_out)
+    B, T, threeD = qkv.shape
+    D = threeD // 3
+    H = n_heads
+    d = D // H
+    m = d * (d - 1) // 2
+    if a_all.shape != (B, T, H * m):
+        raise ValueError(f"a_all must be (B,T,H*m)=({B},{T},{H * m}), got {tuple(a_all.shape)}")
+    _contig(a_all, "a_all"); _contig(qkv, "qkv")
+    if softmax_scale is None:
+        softmax_scale = 1.0 / math.sqrt(d)
+    out_dtype = out_dtype or qkv.dtype
+    hat_dtype = hat_dtype or qkv.dtype
+    if chunk is None:
+        chunk = plan_chunk(B, H, T, d, qkv.device)
+    for t, nm in ((carry_in, "carry_in"), (total_out, "total_out")):
+        if t is not None and (t.dtype != torch.float32 or t.shape != (B * H, d, d) or not t.is_contiguous()):
+            raise ValueError(f"{nm} must be a contiguous fp32 ({B * H},{d},{d}) tensor")
+    lib = _lib.load()
+    hat_code = _dtype_code(hat_dtype)
+    ws_bytes = int(lib.hoa_core_workspace_bytes(B, H, T, d, chunk, hat_code))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=qkv.device)
+    out = torch.empty(B, T, D, dtype=out_dtype, device=qkv.device)
+    _lib.call("hoa_core_forward", _ptr(a_all), _dtype_code(a_all.dtype), float(edge_scale),
+              _ptr(qkv), _dtype_code(qkv.dtype), _ptr(out), _dtype_code(out_dtype), hat_code,
+              float(softmax_scale), _ptr(carry_in), _ptr(total_out), B, H, T, d, int(chunk),
+              _ptr(ws), ws_bytes, _stream(qkv.device))
+    return out
+
+
+# ---------------------------------------------------------------------------
+# individual stages (used by the tests and by the sequence-sharded path)
+# ---------------------------------------------------------------------------
+def link_local(a_all: torch.Tensor, qkv: torch.Tensor, n_heads: int, edge_scale: float,
+               chunk: int) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Kernel (1)+(2) local part -> (R (BH,T,d,d), U (BH,T,3,d), M (BH,K,d,d)), all fp32."""
+    _need_cuda(a_all, qkv)
+    B, T, threeD = qkv.shape
+    H = n_heads
+    d = threeD // 3 // H
+    K = (T + chunk - 1) // chunk
+    _contig(a_all, "a_all"); _contig(qkv, "qkv")
+    dev = qkv.device
+    R = torch.empty(B * H, T, d, d, dtype=torch.float32, device=dev)
+    U = torch.empty(B * H, T, 3, d, dtype=torch.float32, device=dev)
+    M = torch.empty(B * H, K, d, d, dtype=torch.float32, device=dev)
+    _lib.call("hoa_link_local", _ptr(a_all), _dtype_code(a_all.dtype), float(edge_scale), _ptr(qkv),
+              _dtype_code(qkv.dtype), _ptr(R), _ptr(U), _ptr(M), B, H, T, d, int(chunk),
+              _stream(dev))
+    return R, U, M
+
+
+def carry_scan(M: torch.Tensor, carry_in: Optional[torch.Tensor] = None,
+               want_total: bool = False):
+    """C_0 = carry_in (or I), C_{k+1} = M_k C_k -> (C (BH,K,d,d), total (BH,d,d) or None)."""
+    _need_cuda(M, carry_in)
+    BH, K, d, _ = M.shape
+    _contig(M, "M")
+    C = torch.empty_like(M)
+    total = torch.empty(BH, d, d, dtype=torch.float32, device=M.device) if want_total else None
+    _lib.call("hoa_carry_scan", _ptr(M), _ptr(carry_in), _ptr(C), _ptr(total), BH, K, d,
+              _stream(M.device))
+    return C, total
+
+
+def carry_apply(U: torch.Tensor, C: torch.Tensor, chunk: int, hat_dtype: torch.dtype):
+    """q^, k^, v^ (BH,T,d) each, in hat_dtype."""
+    _need_cuda(U, C)
+    BH, T, _, d = U.shape
+    outs = [torch.empty(BH, T, d, dtype=hat_dtype, device=U.device) for _ in range(3)]
+    _lib.call("hoa_carry_apply", _ptr(U), _ptr(C), *(_ptr(o) for o in outs), _dtype_code(hat_dtype),
+              BH, T, d, int(chunk), _stream(U.device))
+    return tuple(outs)
+
+
+def attn_fwd(qh: torch.Tensor, kh: torch.Tensor, vh: torch.Tensor, R: torch.Tensor,
+             C: torch.Tensor, chunk: int, B: int, H: int, softmax_scale: float,
+             out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+    """Kernels (3)+(4): causal attention + out_t = R_t C_k o_t -> (B,T,H*d)."""
+    _need_cuda(qh, kh, vh, R, C)
+    BH, T, d = qh.shape
+    out_dtype = out_dtype or qh.dtype
+    out = torch.empty(B, T, H * d, dtype=out_dtype, device=qh.device)
+    _lib.call("hoa_attn_fwd", _ptr(qh), _ptr(kh), _ptr(vh), _dtype_code(qh.dtype), _ptr(R), _ptr(C),
+              int(chunk), _ptr(out), _dtype_code(out_dtype), float(softmax_scale), B, H, T, d,
+              _stream(qh.device))
+    return out

@@ -1,0 +1,128 @@
+/*
+ * hoa.h — C ABI of the B200 (sm_100a) path-ordered geometric attention forward.
+ *
+ * The library (libhoa.so) implements the causal forward of
+ * PathOrderedGeometricMHA from SiddhiMali/HolonomyAwareAttention between the
+ * PyTorch projections: it takes the edge-MLP output a_all and the qkv
+ * projection, and returns the per-head outputs that feed the `out` Linear.
+ *
+ *   G_t  = expm(skew(edge_scale * a_t))          t = 0 .. T-2   (edge t joins t, t+1)
+ *   P_0  = I,  P_{t+1} = G_t P_t
+ *   q^_t = P_t^T q_t,  k^_t = P_t^T k_t,  v^_t = P_t^T v_t
+ *   o_i  = P_i * sum_{j<=i} softmax_j(q^_i . k^_j * softmax_scale) v^_j
+ *
+ * Layout conventions (row-major, contiguous):
+ *   a_all  (B, T, H, m)    m = d(d-1)/2, row-major strict upper triangle per head
+ *   qkv    (B, T, H, 3d)   per head [q | k | v]  (the reference's qkv(x).view(B,T,H,3d))
+ *   out    (B, T, H, d)    i.e. the (B, T, D) input of the `out` projection
+ *   chain c = b*H + h.  Rotations are always fp32.
+ *
+ * Rules of the ABI: no entry point allocates or synchronises; all work is
+ * enqueued on the caller's stream (`stream` is a cudaStream_t, NULL = legacy
+ * default stream).  Scratch comes from the caller through `workspace`
+ * (hoa_core_workspace_bytes).  Every entry point returns a hoa_status.
+ * Entry points are thread-compatible: they keep no mutable global state.
+ */
+#ifndef HOA_H_
+#define HOA_H_
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  HOA_OK = 0,
+  HOA_ERR_INVALID_ARG = 1,   /* null pointer, bad shape, misaligned pointer */
+  HOA_ERR_UNSUPPORTED = 2,   /* head dim or dtype outside the compiled set  */
+  HOA_ERR_LAUNCH = 3,        /* CUDA launch failed (cudaGetLastError)       */
+  HOA_ERR_WORKSPACE = 4,     /* workspace too small                          */
+  HOA_ERR_TIMEOUT = 5        /* a bounded device-side wait gave up           */
+} hoa_status;
+
+typedef enum { HOA_F32 = 0, HOA_BF16 = 1 } hoa_dtype;
+
+/* Library facts. */
+int hoa_abi_version(void);
+int hoa_max_head_dim(void);
+const char* hoa_status_string(int status);
+
+/* Chunk length used to split each (b,h) rotation chain into independent
+ * chunks (composed locally, then joined by hoa_carry_scan).  `num_sms` is the
+ * device's SM count.  Returns a multiple of 16 in [16, T] (or T when T < 16). */
+int hoa_plan_chunk(int B, int H, int T, int d, int num_sms);
+
+/* Bytes of scratch hoa_core_forward needs. */
+size_t hoa_core_workspace_bytes(int B, int H, int T, int d, int chunk, int hat_dtype);
+
+/*
+ * Whole core region in one call: kernels (1)-(4).
+ * Replaces the reference's core region between the projections:
+ *   core/attention_fast_chunked.py:86-95   so_exp(skew_from_vec(a)) + prefix loop
+ *   core/attention_fast_chunked.py:108-110 transport q^, k^, v^
+ *   core/attention_fast_chunked.py:119-171 causal fold and out_i = P_i o_i
+ * (kernel/attention_kernel.py:215-216 `_geometry` + `HoloAttnFn.apply`).
+ * a_dtype / qkv_dtype / out_dtype: HOA_F32 or HOA_BF16.  hat_dtype is the
+ * dtype of the transported q^/k^/v^ fed to attention (HOA_BF16 for bf16
+ * activations, HOA_F32 for fp32).  `carry_in` (nullable, (B*H, d, d) fp32)
+ * is P at the first position (a previous shard's product; NULL = identity);
+ * `total_out` (nullable, (B*H, d, d)) receives the product through the last
+ * edge t = T-1 (for a full sequence that edge is the closing edge, and
+ * total_out is the holonomy G_close P_{T-1}, core/attention_fast_chunked.py:95).
+ */
+int hoa_core_forward(const void* a_all, int a_dtype, float edge_scale,
+                     const void* qkv, int qkv_dtype,
+                     void* out, int out_dtype, int hat_dtype, float softmax_scale,
+                     const float* carry_in, float* total_out,
+                     int B, int H, int T, int d, int chunk,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Kernels (1)+(2), local part: per (chain, chunk) unit, builds
+ * G_t = expm(skew(edge_scale*a_t)) in fp32 and the local products
+ * R_{t0} = I, R_{t+1} = G_t R_t over the chunk's edges.
+ * Writes R (B*H, T, d, d) fp32 — R_t for every position —, the locally
+ * transported vectors U (B*H, T, 3, d) fp32 = R_t^T [q_t, k_t, v_t], and the
+ * chunk totals M (B*H, K, d, d) = R after the chunk's last edge.
+ * Replaces core/attention_fast_chunked.py:86-94 (with core/utils.py:4-52)
+ * and the transport at :108-110, split into independent chunks.
+ */
+int hoa_link_local(const void* a_all, int a_dtype, float edge_scale,
+                   const void* qkv, int qkv_dtype,
+                   float* R, float* U, float* M,
+                   int B, int H, int T, int d, int chunk, void* stream);
+
+/*
+ * Kernel (2), carry: C_0 = carry_in (or I), C_{k+1} = M_k C_k for the K
+ * chunks of each chain; writes C (B*H, K, d, d) and, if total_out != NULL,
+ * C_K.  Joins the chunks so that P_t = R_t C_{t/chunk}
+ * (core/attention_fast_chunked.py:91-94 re-associated).
+ */
+int hoa_carry_scan(const float* M, const float* carry_in, float* C, float* total_out,
+                   int BH, int K, int d, void* stream);
+
+/*
+ * Kernel (2), transport: q^_t = C_k^T U_q[t] (likewise k, v), written as
+ * (B*H, T, d) in hat_dtype.  Completes core/attention_fast_chunked.py:108-110.
+ */
+int hoa_carry_apply(const float* U, const float* C, void* qh, void* kh, void* vh,
+                    int hat_dtype, int BH, int T, int d, int chunk, void* stream);
+
+/*
+ * Kernels (3)+(4): causal online-softmax attention on q^/k^/v^ (B*H, T, d)
+ * with fp32 accumulation, then out_t = R_t (C_{t/chunk} o_t) written to
+ * out (B, T, H, d) in out_dtype.
+ * Replaces core/attention_fast_chunked.py:119-171 (kernel/attention_kernel.py:122-134
+ * run_fwd_kernel) for the causal tril mask.
+ */
+int hoa_attn_fwd(const void* qh, const void* kh, const void* vh, int hat_dtype,
+                 const float* R, const float* C, int chunk,
+                 void* out, int out_dtype, float softmax_scale,
+                 int B, int H, int T, int d, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HOA_H_ */

@@ -1,0 +1,75 @@
+"""The C-ABI library: it loads, exports every symbol include/hoa.h declares,
+and rejects bad arguments before touching the GPU (no compute calls here)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from holonomyawareattention_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "hoa.h")
+
+
+def declared_symbols():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(hoa_[a-z_0-9]+)\s*\(", src)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from holonomyawareattention_b200 import _build
+    _build.build()
+    return _lib.load()
+
+
+def test_header_symbols_exported(lib):
+    syms = declared_symbols()
+    assert len(syms) >= 10
+    for s in syms:
+        assert hasattr(lib, s), f"{s} declared in hoa.h but not exported"
+        assert s in _lib.SIGNATURES, f"{s} has no ctypes signature"
+
+
+def test_library_facts(lib):
+    assert lib.hoa_abi_version() == 1
+    assert lib.hoa_max_head_dim() == 120
+    assert lib.hoa_status_string(0) == b"ok"
+    assert b"workspace" in lib.hoa_status_string(4)
+
+
+@pytest.mark.parametrize("B,H,T,d,sms", [(16, 16, 4096, 96, 148), (64, 4, 512, 48, 148),
+                                          (128, 24, 2048, 120, 148), (1, 16, 65536, 96, 148),
+                                          (2, 4, 12, 8, 148), (1, 1, 1, 8, 148)])
+def test_plan_chunk(lib, B, H, T, d, sms):
+    c = lib.hoa_plan_chunk(B, H, T, d, sms)
+    assert 1 <= c <= max(T, 1)
+    if T >= 16:
+        assert c % 16 == 0 or c == T
+
+
+def test_workspace_bytes(lib):
+    n = lib.hoa_core_workspace_bytes(16, 16, 4096, 96, 832, _lib.HOA_BF16)
+    # R dominates: B*H*T*d*d*4 bytes
+    assert n >= 16 * 16 * 4096 * 96 * 96 * 4
+    assert lib.hoa_core_workspace_bytes(0, 16, 4096, 96, 832, 1) == 0
+
+
+def test_invalid_arguments_rejected_without_gpu(lib):
+    null = None
+    # null pointers -> HOA_ERR_INVALID_ARG (1) before any CUDA call
+    assert lib.hoa_link_local(null, 0, 1.0, null, 0, null, null, null, 1, 1, 4, 8, 4, null) == 1
+    assert lib.hoa_attn_fwd(null, null, null, 0, null, null, 4, null, 0, 1.0, 1, 1, 4, 8, null) == 1
+    assert lib.hoa_carry_scan(null, null, null, null, 1, 1, 8, null) == 1
+    # unsupported head dim -> HOA_ERR_UNSUPPORTED (2)
+    dummy = ctypes.c_void_p(16)
+    assert lib.hoa_link_local(dummy, 0, 1.0, dummy, 0, dummy, dummy, dummy, 1, 1, 4, 200, 4, null) == 2
+    # bad dtype code
+    assert lib.hoa_link_local(dummy, 7, 1.0, dummy, 0, dummy, dummy, dummy, 1, 1, 4, 8, 4, null) == 2
+    # workspace too small -> HOA_ERR_WORKSPACE (4)
+    assert lib.hoa_core_forward(dummy, 0, 1.0, dummy, 0, dummy, 0, 0, 1.0, null, null,
+                                1, 1, 4, 8, 4, dummy, 16, null) == 4
+    with pytest.raises(_lib.HoaError):
+        _lib.check("hoa_link_local", 2)

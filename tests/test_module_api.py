@@ -1,0 +1,57 @@
+"""Drop-in API of PathOrderedGeometricMHA (CPU: construction, parameters, gating)."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from holonomyawareattention_b200 import PathOrderedGeometricMHA
+from oracle.seeded import checksums
+
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def test_constructor_errors():
+    with pytest.raises(ValueError):
+        PathOrderedGeometricMHA(30, n_heads=4)
+    with pytest.raises(ValueError):
+        PathOrderedGeometricMHA(32, n_heads=4, mode="ring")
+
+
+def test_attributes_and_state_dict():
+    m = PathOrderedGeometricMHA(192, n_heads=4, edge_scale=0.05)
+    assert (m.h, m.d, m.m_dim, m.edge_scale, m.mode, m.link_mode) == (4, 48, 1128, 0.05, "causal",
+                                                                        "interaction")
+    assert abs(m.scale - 48 ** -0.5) < 1e-12
+    shapes = {k: tuple(v.shape) for k, v in m.state_dict().items()}
+    assert list(shapes) == ["qkv.weight", "out.weight", "gqproj.weight", "gkproj.weight",
+                            "edge_mlp.0.weight", "edge_mlp.0.bias", "edge_mlp.2.weight",
+                            "edge_mlp.2.bias"]
+    assert shapes["edge_mlp.2.weight"] == (1128 * 4, 768)
+    assert shapes["qkv.weight"] == (576, 192)
+
+
+@pytest.mark.parametrize("name", ["tiny_es01", "d48_L40", "d96_L32"])
+def test_seeded_init_matches_reference(name):
+    """Same creation order as the reference => identical seeded default init."""
+    z = np.load(os.path.join(GOLD, name + ".npz"))
+    torch.manual_seed(int(z["seed"]))
+    m = PathOrderedGeometricMHA(int(z["D"]), n_heads=int(z["H"]), edge_scale=float(z["edge_scale"]))
+    for k, v in checksums(m.state_dict()).items():
+        np.testing.assert_allclose(v, z["cs:" + k], rtol=1e-9, atol=1e-12)
+    x = torch.randn(int(z["B"]), int(z["L"]), int(z["D"]))
+    np.testing.assert_array_equal(x.numpy(), z["x"])
+
+
+def test_unsupported_inputs_raise():
+    m = PathOrderedGeometricMHA(32, n_heads=4).eval()
+    x = torch.randn(2, 12, 32)
+    tril = torch.tril(torch.ones(12, 12, dtype=torch.bool))
+    with torch.no_grad():
+        with pytest.raises(NotImplementedError, match="CUDA"):
+            m(x, attn_mask=tril)
+    inert = PathOrderedGeometricMHA(32, n_heads=4, mode="inert").eval()
+    with torch.no_grad(), pytest.raises(NotImplementedError, match="causal"):
+        inert(x, attn_mask=tril)
+    with torch.no_grad(), pytest.raises(NotImplementedError, match="geometry"):
+        m(x, attn_mask=tril, return_geometry=True)

@@ -1,0 +1,175 @@
+"""GPU parity of the sm_100a path against the oracle and the reference's golden vectors.
+
+Bars (from the task): rel-L2 <= 1e-5 for fp32 inputs, <= 2e-2 for bf16 inputs,
+against the reference PyTorch path on identical seeded inputs and weights.
+Everything here calls the CUDA library through the C ABI (ops / module).
+"""
+import math
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from holonomyawareattention_b200 import PathOrderedGeometricMHA, ops
+from oracle import holonomy_oracle as O
+from oracle import torch_ref
+from oracle.seeded import params_of, seeded_case
+
+pytestmark = pytest.mark.gpu
+
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+FP32_TOL = 1e-5
+BF16_TOL = 2e-2
+DEV = "cuda"
+
+
+def load(name):
+    return np.load(os.path.join(GOLD, name + ".npz"))
+
+
+def fixture_module(z, dtype=torch.float32):
+    D, H, seed, B, L = (int(z[k]) for k in ("D", "H", "seed", "B", "L"))
+    m = PathOrderedGeometricMHA(D, n_heads=H, edge_scale=float(z["edge_scale"]))
+    if "w:qkv.weight" in z.files:
+        m.load_state_dict({k[2:]: torch.from_numpy(z[k]) for k in z.files if k.startswith("w:")})
+    else:
+        sd, _ = seeded_case(D, H, seed, B, L, bool(int(z["bf16_round"])))
+        m.load_state_dict(sd)
+    return m.to(device=DEV, dtype=dtype).eval()
+
+
+def tril(L):
+    return torch.tril(torch.ones(L, L, dtype=torch.bool, device=DEV))
+
+
+def run(m, x):
+    with torch.no_grad():
+        y, geom = m(x, attn_mask=tril(x.shape[1]))
+    assert geom is None
+    return y.float().cpu().numpy()
+
+
+@pytest.mark.parametrize("name", ["tiny_es01", "tiny_es15", "d48_L40", "d96_L32", "d120_L24", "c1"])
+def test_golden_fp32(name):
+    z = load(name)
+    m = fixture_module(z)
+    y = run(m, torch.from_numpy(z["x"]).to(DEV))
+    assert O.rel_l2(y, z["y_chunked_f64"]) <= FP32_TOL
+    assert O.rel_l2(y, z["y_chunked_f32"]) <= FP32_TOL
+    if "y_orig_f32" in z.files:     # core/attention.py, the O(L^3) original
+        assert O.rel_l2(y, z["y_orig_f32"]) <= FP32_TOL
+
+
+def test_golden_bf16():
+    z = load("bf16_d48_L64")
+    m = fixture_module(z, torch.bfloat16)
+    y = run(m, torch.from_numpy(z["x"]).to(DEV, torch.bfloat16))
+    assert O.rel_l2(y, z["y_chunked_f64"]) <= BF16_TOL
+
+
+@pytest.mark.parametrize("chunk", [1, 5, 16, 40])
+def test_chunking_invariance(chunk):
+    z = load("d48_L40")
+    m = fixture_module(z)
+    x = torch.from_numpy(z["x"]).to(DEV)
+    m.chunk = None
+    y0 = run(m, x)
+    m.chunk = chunk
+    y1 = run(m, x)
+    assert O.rel_l2(y1, y0) < 2e-6
+    assert O.rel_l2(y1, z["y_chunked_f64"]) <= FP32_TOL
+
+
+@pytest.mark.parametrize("d", [8, 16, 32, 48, 64, 96, 120])
+@pytest.mark.parametrize("L", [1, 2, 17, 65])
+def test_lengths_and_head_dims(d, L):
+    H = 3                                   # odd B*H
+    D = d * H
+    sd, x = seeded_case(D, H, seed=100 + d + L, B=1, L=L)
+    m = PathOrderedGeometricMHA(D, n_heads=H, edge_scale=0.3)
+    m.load_state_dict(sd)
+    m = m.to(DEV).eval()
+    y = run(m, x.to(DEV))
+    ref = O.forward(params_of(sd), x.numpy().astype(np.float64), H, 0.3, np.float64)
+    assert np.isfinite(y).all()
+    assert O.rel_l2(y, ref) <= FP32_TOL
+
+
+def test_link_stage_geometry_vs_oracle():
+    """P_t = R_t C_k and the holonomy against the float64 oracle (kernels 1+2)."""
+    z = load("tiny_es15")
+    sd = {k[2:]: torch.from_numpy(z[k]) for k in z.files if k.startswith("w:")}
+    H, es = int(z["H"]), float(z["edge_scale"])
+    x = torch.from_numpy(z["x"])
+    p = params_of(sd)
+    a_unscaled = O.edge_generators(p, x.numpy().astype(np.float64), H, 1.0)   # (B,H,L,m)
+    B, _, L, mm = a_unscaled.shape
+    d = x.shape[-1] // H
+    a_dev = torch.from_numpy(a_unscaled.transpose(0, 2, 1, 3).reshape(B, L, H * mm)).float().to(DEV)
+    qkv = torch.from_numpy((x.numpy().astype(np.float64) @ p.qkv.T)).float().to(DEV).contiguous()
+    for chunk in (1, 4, L):
+        R, U, M = ops.link_local(a_dev, qkv, H, es, chunk)
+        C, total = ops.carry_scan(M, want_total=True)
+        k_of_t = torch.arange(L, device=DEV) // chunk
+        P = torch.einsum("ntij,ntjk->ntik", R, C[:, k_of_t]).view(B, H, L, d, d).cpu().numpy()
+        assert O.rel_l2(P, z["P_f64"]) < 2e-6
+        assert O.rel_l2(total.view(B, H, d, d).cpu().numpy(), z["Hol_f64"]) < 2e-6
+        I = np.eye(d)
+        assert np.abs(np.swapaxes(P, -1, -2) @ P - I).max() < 1e-5
+
+
+def test_attention_stage_vs_torch():
+    """Kernel (3)+(4) alone: identity rotations reduce it to causal attention."""
+    torch.manual_seed(0)
+    B, H, T, d = 2, 3, 150, 96
+    qh, kh, vh = (torch.randn(B * H, T, d, device=DEV) for _ in range(3))
+    R = torch.eye(d, device=DEV).expand(B * H, T, d, d).contiguous()
+    C = torch.eye(d, device=DEV).expand(B * H, 1, d, d).contiguous()
+    out = ops.attn_fwd(qh, kh, vh, R, C, T, B, H, 1 / math.sqrt(d), torch.float32)
+    s = (qh @ kh.transpose(1, 2)) / math.sqrt(d)
+    s = s.masked_fill(~torch.tril(torch.ones(T, T, dtype=torch.bool, device=DEV)), float("-inf"))
+    ref = (torch.softmax(s.double(), -1) @ vh.double()).view(B, H, T, d).transpose(1, 2).reshape(B, T, H * d)
+    assert O.rel_l2(out.cpu().numpy(), ref.cpu().numpy()) < 1e-6
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_config2_full_size(dtype):
+    """B=64, T=512, d_model=192, H=4 against the torch restatement (fp32)."""
+    B, T, D, H, es = 64, 512, 192, 4, 0.05
+    sd, x = seeded_case(D, H, seed=0, B=B, L=T, bf16_round=dtype == torch.bfloat16)
+    m = PathOrderedGeometricMHA(D, n_heads=H, edge_scale=es)
+    m.load_state_dict(sd)
+    m = m.to(DEV, dtype).eval()
+    y = run(m, x.to(DEV, dtype))
+    ref = torch_ref.module_forward(sd, x.to(DEV), H, es, torch.float32, batch_slice=16).cpu().numpy()
+    assert O.rel_l2(y, ref) <= (FP32_TOL if dtype == torch.float32 else BF16_TOL)
+
+
+def test_config3_slice_bf16():
+    """configs[2] shape (T=4096, d_model=1536, H=16, bf16) on two batch rows vs fp32 torch restatement."""
+    B, T, D, H, es = 2, 4096, 1536, 16, 0.05
+    sd, x = seeded_case(D, H, seed=0, B=B, L=T, bf16_round=True)
+    m = PathOrderedGeometricMHA(D, n_heads=H, edge_scale=es)
+    m.load_state_dict(sd)
+    m = m.to(DEV, torch.bfloat16).eval()
+    y = run(m, x.to(DEV, torch.bfloat16))
+    ref = torch_ref.module_forward(sd, x.to(DEV), H, es, torch.float32, batch_slice=1).cpu().numpy()
+    err = O.rel_l2(y, ref)
+    print(f"c3 slice bf16 rel-L2 {err:.3e}")
+    assert err <= BF16_TOL
+
+
+def test_deterministic_and_rejects():
+    z = load("d96_L32")
+    m = fixture_module(z)
+    x = torch.from_numpy(z["x"]).to(DEV)
+    assert np.array_equal(run(m, x), run(m, x))
+    L = x.shape[1]
+    with torch.no_grad():
+        with pytest.raises(NotImplementedError):
+            m(x, attn_mask=None)
+        bad = tril(L).clone()
+        bad[5, 0] = False
+        with pytest.raises(NotImplementedError):
+            m(x, attn_mask=bad)
