@@ -31,9 +31,14 @@ SIGNATURES = {
     "hoa_carry_scan": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
                                c_void_p]),
     "hoa_carry_apply": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,
-                                c_int, c_int, c_int, c_void_p]),
-    "hoa_attn_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int,
-                             c_void_p, c_int, c_float, c_int, c_int, c_int, c_int, c_void_p]),
+                                c_int, c_int, c_int, c_int, c_void_p]),
+    "hoa_vt_stride": (c_int, [c_int]),
+    "hoa_attn_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_float, c_int, c_int,
+                             c_int, c_void_p]),
+    "hoa_attn_tc_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_int,
+                                c_int, c_int, c_void_p]),
+    "hoa_out_transport": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_int,
+                                  c_int, c_int, c_int, c_void_p]),
 }
 
 _lock = threading.Lock()

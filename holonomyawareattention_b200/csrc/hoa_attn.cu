@@ -1,12 +1,13 @@
-// Kernels (3) and (4): causal online-softmax attention over the transported
-// q^, k^, v^ and the inverse transport out_t = P_t o_t with P_t = R_t C_{t/chunk}.
+// Kernel (3), fp32 path: causal online-softmax attention over the transported
+// q^, k^, v^, written as the normalised o (fp32, (B*H, T, d)); the inverse
+// transport (kernel 4) follows in hoa_transport.cu.
 //
 // Reference semantics (SiddhiMali/HolonomyAwareAttention):
 //   scores q^_i . k^_j * scale, tril mask with finfo.min, online softmax,
-//   o / l.clamp_min(1e-20), out_i = P_i o_i     core/attention_fast_chunked.py:119-171
+//   o / l.clamp_min(1e-20)                    core/attention_fast_chunked.py:119-168
 //
-// This file holds the fp32 (SIMT) variant: q^/k^/v^ in fp32 or bf16, every
-// product and the softmax in fp32.  One CTA per (query tile of 64, chain).
+// SIMT variant: q^/k^/v^ in fp32 (or bf16), every product and the softmax in
+// fp32, so fp32 inputs keep fp32 accuracy.  One CTA per (64-query tile, chain).
 #include "hoa_common.cuh"
 
 namespace hoa {
@@ -23,9 +24,8 @@ template <int DA> struct AttnCfg {
 
 struct AttnArgs {
   const void* qh; const void* kh; const void* vh; int hat_dtype;
-  const float* R; const float* C; int chunk, K;
-  void* out; int out_dtype; float scale;
-  int B, H, T, d;
+  float* o; float scale;
+  int T, d;
 };
 
 template <int N>
@@ -48,12 +48,6 @@ HOA_DEVICE void lds4(const float* __restrict__ p, float (&v)[N]) {
   }
 }
 
-HOA_DEVICE float warp_sum(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
-}
-
 template <int DA>
 __global__ void __launch_bounds__(kAttnThreads) attn_fwd_simt_kernel(AttnArgs p) {
   using Cf = AttnCfg<DA>;
@@ -68,7 +62,6 @@ __global__ void __launch_bounds__(kAttnThreads) attn_fwd_simt_kernel(AttnArgs p)
   const int ty = tid / 16, tx = tid % 16;
   const int r0 = ty * 4, c0 = tx * 4;
   const int chain = blockIdx.y;
-  const int b = chain / p.H, h = chain % p.H;
   const int qtile = gridDim.x - 1 - blockIdx.x;     // heaviest causal tiles first
   const int q0 = qtile * kBQ;
   const int d = p.d, T = p.T;
@@ -162,50 +155,28 @@ __global__ void __launch_bounds__(kAttnThreads) attn_fwd_simt_kernel(AttnArgs p)
     }
   }
 
-  // ---- epilogue: o / l, then out_t = R_t (C_k o_t) --------------------------
-  __syncthreads();
-  float* Os = Kt;                   // [kBQ][DA]
-  float* Wv = Qt;                   // [8 warps][DA]
+  // ---- epilogue: o / l ------------------------------------------------------
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
+    const int t = q0 + r0 + i;
+    if (t >= T) continue;
     const float inv = 1.f / fmaxf(lrow[i], 1e-20f);
+    float* orow = p.o + ((long long)chain * T + t) * d;
 #pragma unroll
-    for (int j = 0; j < CPT; ++j) Os[(r0 + i) * DA + tx * CPT + j] = o[i][j] * inv;
-  }
-  __syncthreads();
-  const int warp = tid / 32, lane = tid % 32;
-  float* wv = Wv + warp * DA;
-  for (int rr = warp; rr < kBQ; rr += kAttnThreads / 32) {
-    const int t = q0 + rr;
-    if (t >= T) break;
-    const float* orow = Os + rr * DA;
-    const float* Cg = p.C + ((long long)chain * p.K + t / p.chunk) * d * d;
-    const float* Rg = p.R + ((long long)chain * T + t) * d * d;
-    for (int e = 0; e < d; ++e) {
-      float part = 0.f;
-      for (int f = lane; f < d; f += 32) part = fmaf(Cg[e * d + f], orow[f], part);
-      part = warp_sum(part);
-      if (lane == 0) wv[e] = part;
+    for (int j = 0; j < CPT; ++j) {
+      const int e = tx * CPT + j;
+      if (e < d) orow[e] = o[i][j] * inv;
     }
-    __syncwarp();
-    const long long obase = (((long long)b * T + t) * p.H + h) * d;
-    for (int e = 0; e < d; ++e) {
-      float part = 0.f;
-      for (int f = lane; f < d; f += 32) part = fmaf(Rg[e * d + f], wv[f], part);
-      part = warp_sum(part);
-      if (lane == 0) store_elem(p.out, obase + e, p.out_dtype, part);
-    }
-    __syncwarp();
   }
 }
 
 template <int DA>
-int launch_attn(const AttnArgs& a, cudaStream_t s) {
+int launch_attn(const AttnArgs& a, int BH, cudaStream_t s) {
   using Cf = AttnCfg<DA>;
   if (cudaFuncSetAttribute(attn_fwd_simt_kernel<DA>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)Cf::kSmem) != cudaSuccess)
     return HOA_ERR_LAUNCH;
-  dim3 grid((unsigned)ceil_div(a.T, kBQ), (unsigned)(a.B * a.H));
+  dim3 grid((unsigned)ceil_div(a.T, kBQ), (unsigned)BH);
   attn_fwd_simt_kernel<DA><<<grid, kAttnThreads, Cf::kSmem, s>>>(a);
   return launch_status();
 }
@@ -215,27 +186,22 @@ int launch_attn(const AttnArgs& a, cudaStream_t s) {
 using namespace hoa;
 
 extern "C" int hoa_attn_fwd(const void* qh, const void* kh, const void* vh, int hat_dtype,
-                            const float* R, const float* C, int chunk, void* out, int out_dtype,
-                            float softmax_scale, int B, int H, int T, int d, void* stream) {
-  if (!qh || !kh || !vh || !R || !C || !out || B < 1 || H < 1 || T < 1 || d < 1 || chunk < 1)
-    return HOA_ERR_INVALID_ARG;
-  if ((hat_dtype != HOA_F32 && hat_dtype != HOA_BF16) ||
-      (out_dtype != HOA_F32 && out_dtype != HOA_BF16))
-    return HOA_ERR_UNSUPPORTED;
-  if ((long long)B * H > 65535) return HOA_ERR_UNSUPPORTED;
-  AttnArgs a{qh, kh, vh, hat_dtype, R, C, chunk, ceil_div(T, chunk), out, out_dtype,
-             softmax_scale, B, H, T, d};
+                            float* o, float softmax_scale, int BH, int T, int d, void* stream) {
+  if (!qh || !kh || !vh || !o || BH < 1 || T < 1 || d < 1) return HOA_ERR_INVALID_ARG;
+  if (hat_dtype != HOA_F32 && hat_dtype != HOA_BF16) return HOA_ERR_UNSUPPORTED;
+  if (BH > 65535) return HOA_ERR_UNSUPPORTED;
+  AttnArgs a{qh, kh, vh, hat_dtype, o, softmax_scale, T, d};
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int da = ((d + 15) / 16) * 16;
   switch (da) {
-    case 16: return launch_attn<16>(a, s);
-    case 32: return launch_attn<32>(a, s);
-    case 48: return launch_attn<48>(a, s);
-    case 64: return launch_attn<64>(a, s);
-    case 80: return launch_attn<80>(a, s);
-    case 96: return launch_attn<96>(a, s);
-    case 112: return launch_attn<112>(a, s);
-    case 128: return launch_attn<128>(a, s);
+    case 16: return launch_attn<16>(a, BH, s);
+    case 32: return launch_attn<32>(a, BH, s);
+    case 48: return launch_attn<48>(a, BH, s);
+    case 64: return launch_attn<64>(a, BH, s);
+    case 80: return launch_attn<80>(a, BH, s);
+    case 96: return launch_attn<96>(a, BH, s);
+    case 112: return launch_attn<112>(a, BH, s);
+    case 128: return launch_attn<128>(a, BH, s);
     default: return HOA_ERR_UNSUPPORTED;
   }
 }

@@ -365,15 +365,19 @@ carry_scan_kernel(const float* __restrict__ M, const float* __restrict__ carry_i
 }
 
 // hat_v[t] = C_k^T U_v[t] for v in {q, k, v}.  One CTA per (chain, chunk).
+// q^ and k^ are written (B*H, T, d); v^ likewise, or transposed as
+// (B*H, d, vt_stride) when vt_stride > 0 (the K-major layout the tensor-core
+// attention reads for its P V product).
 constexpr int kApplyThreads = 256;
-constexpr int kApplyPos = 8;   // positions staged per step
+constexpr int kApplyPos = 32;   // positions staged per step
 
 __global__ void __launch_bounds__(kApplyThreads)
 carry_apply_kernel(const float* __restrict__ U, const float* __restrict__ Cin, void* qh, void* kh,
-                   void* vh, int hat_dtype, int T, int d, int chunk, int K) {
+                   void* vh, int hat_dtype, int vt_stride, int T, int d, int chunk, int K) {
   extern __shared__ __align__(16) float smem[];
-  float* Cs = smem;                 // d*d, row-major
-  float* Us = Cs + d * d;           // kApplyPos * 3 * d
+  float* Cs = smem;                      // d*d, row-major
+  float* Us = Cs + d * d;                // kApplyPos * 3 * d
+  float* Vt = Us + kApplyPos * 3 * d;    // d * kApplyPos (transposed v^)
   const int tid = threadIdx.x;
   const int chain = blockIdx.x / K;
   const int kc = blockIdx.x % K;
@@ -381,6 +385,7 @@ carry_apply_kernel(const float* __restrict__ U, const float* __restrict__ Cin, v
   const float* Cg = Cin + ((long long)chain * K + kc) * d * d;
   for (int i = tid; i < d * d; i += kApplyThreads) Cs[i] = Cg[i];
   void* outs[3] = {qh, kh, vh};
+  const int nvec = vt_stride > 0 ? 2 : 3;
   for (int tb = t0; tb < t1; tb += kApplyPos) {
     const int np = min(kApplyPos, t1 - tb);
     __syncthreads();
@@ -392,7 +397,16 @@ carry_apply_kernel(const float* __restrict__ U, const float* __restrict__ Cin, v
       const float* u = Us + (pp * 3 + v) * d;
       float s = 0.f;
       for (int r = 0; r < d; ++r) s = fmaf(Cs[r * d + e], u[r], s);
-      store_elem(outs[v], ((long long)chain * T + tb + pp) * d + e, hat_dtype, s);
+      if (v < nvec) store_elem(outs[v], ((long long)chain * T + tb + pp) * d + e, hat_dtype, s);
+      else Vt[e * kApplyPos + pp] = s;
+    }
+    if (vt_stride > 0) {
+      __syncthreads();
+      for (int i = tid; i < d * kApplyPos; i += kApplyThreads) {
+        const int e = i / kApplyPos, pp = i % kApplyPos;
+        if (pp < np)
+          store_elem(vh, ((long long)chain * d + e) * vt_stride + tb + pp, hat_dtype, Vt[i]);
+      }
     }
   }
 }
@@ -497,19 +511,21 @@ extern "C" int hoa_carry_scan(const float* M, const float* carry_in, float* C, f
 }
 
 extern "C" int hoa_carry_apply(const float* U, const float* C, void* qh, void* kh, void* vh,
-                               int hat_dtype, int BH, int T, int d, int chunk, void* stream) {
+                               int hat_dtype, int vt_stride, int BH, int T, int d, int chunk,
+                               void* stream) {
   if (!U || !C || !qh || !kh || !vh || BH < 1 || T < 1 || d < 1 || chunk < 1)
     return HOA_ERR_INVALID_ARG;
   if (!valid_dtype(hat_dtype)) return HOA_ERR_UNSUPPORTED;
   if (padded_dim(d) == 0) return HOA_ERR_UNSUPPORTED;
+  if (vt_stride != 0 && vt_stride < T) return HOA_ERR_INVALID_ARG;
   const int K = ceil_div(T, chunk);
-  const size_t smem = (size_t)(d * d + kApplyPos * 3 * d) * sizeof(float);
+  const size_t smem = (size_t)(d * d + kApplyPos * 3 * d + d * kApplyPos) * sizeof(float);
   if (cudaFuncSetAttribute(carry_apply_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)smem) != cudaSuccess)
     return HOA_ERR_LAUNCH;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   carry_apply_kernel<<<(unsigned)((long long)BH * K), kApplyThreads, smem, s>>>(
-      U, C, qh, kh, vh, hat_dtype, T, d, chunk, K);
+      U, C, qh, kh, vh, hat_dtype, vt_stride, T, d, chunk, K);
   return launch_status();
 }
 
@@ -518,24 +534,34 @@ extern "C" int hoa_carry_apply(const float* U, const float* C, void* qh, void* k
 // ---------------------------------------------------------------------------
 namespace {
 struct CoreLayout {
-  size_t R, U, M, C, qh, kh, vh, total;
+  size_t status, R, U, M, C, qh, kh, vh, o, total;
+  bool tc;
+  int vt_stride;
 };
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// The tensor-core attention serves bf16 hats with d % 8 == 0, d <= 128 (TMA
+// row alignment, one TMEM accumulator); fp32 hats keep the fp32 SIMT attention.
+bool use_tc(int hat_dtype, int d) { return hat_dtype == HOA_BF16 && d % 8 == 0 && d <= 128; }
 
 CoreLayout core_layout(int B, int H, int T, int d, int chunk, int hat_dtype) {
   const size_t BH = (size_t)B * H;
   const size_t K = (size_t)((T + chunk - 1) / chunk);
   const size_t hs = hat_dtype == HOA_BF16 ? 2 : 4;
   CoreLayout L{};
+  L.tc = use_tc(hat_dtype, d);
+  L.vt_stride = L.tc ? hoa_vt_stride(T) : 0;
   size_t off = 0;
+  L.status = off; off = align256(off + 256);
   L.R = off; off = align256(off + BH * T * d * d * sizeof(float));
   L.U = off; off = align256(off + BH * T * 3 * d * sizeof(float));
   L.M = off; off = align256(off + BH * K * d * d * sizeof(float));
   L.C = off; off = align256(off + BH * K * d * d * sizeof(float));
   L.qh = off; off = align256(off + BH * T * d * hs);
   L.kh = off; off = align256(off + BH * T * d * hs);
-  L.vh = off; off = align256(off + BH * T * d * hs);
+  L.vh = off; off = align256(off + BH * (L.tc ? (size_t)L.vt_stride * d : (size_t)T * d) * hs);
+  L.o = off; off = align256(off + BH * T * d * sizeof(float));
   L.total = off;
   return L;
 }
@@ -560,6 +586,7 @@ extern "C" int hoa_core_forward(const void* a_all, int a_dtype, float edge_scale
   const CoreLayout L = core_layout(B, H, T, d, chunk, hat_dtype);
   if (workspace_bytes < L.total) return HOA_ERR_WORKSPACE;
   char* w = static_cast<char*>(workspace);
+  int* status = reinterpret_cast<int*>(w + L.status);
   float* R = reinterpret_cast<float*>(w + L.R);
   float* U = reinterpret_cast<float*>(w + L.U);
   float* M = reinterpret_cast<float*>(w + L.M);
@@ -567,14 +594,19 @@ extern "C" int hoa_core_forward(const void* a_all, int a_dtype, float edge_scale
   void* qh = w + L.qh;
   void* kh = w + L.kh;
   void* vh = w + L.vh;
+  float* o = reinterpret_cast<float*>(w + L.o);
   const int K = ceil_div(T, chunk);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(status, 0, sizeof(int), s) != cudaSuccess) return HOA_ERR_LAUNCH;
   int st = hoa_link_local(a_all, a_dtype, edge_scale, qkv, qkv_dtype, R, U, M, B, H, T, d, chunk,
                           stream);
   if (st != HOA_OK) return st;
   st = hoa_carry_scan(M, carry_in, C, total_out, B * H, K, d, stream);
   if (st != HOA_OK) return st;
-  st = hoa_carry_apply(U, C, qh, kh, vh, hat_dtype, B * H, T, d, chunk, stream);
+  st = hoa_carry_apply(U, C, qh, kh, vh, hat_dtype, L.vt_stride, B * H, T, d, chunk, stream);
   if (st != HOA_OK) return st;
-  return hoa_attn_fwd(qh, kh, vh, hat_dtype, R, C, chunk, out, out_dtype, softmax_scale, B, H, T,
-                      d, stream);
+  st = L.tc ? hoa_attn_tc_fwd(qh, kh, vh, o, status, softmax_scale, B * H, T, d, stream)
+            : hoa_attn_fwd(qh, kh, vh, hat_dtype, o, softmax_scale, B * H, T, d, stream);
+  if (st != HOA_OK) return st;
+  return hoa_out_transport(o, R, C, chunk, out, out_dtype, B, H, T, d, stream);
 }

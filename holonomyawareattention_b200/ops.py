@@ -126,25 +126,74 @@ def carry_scan(M: torch.Tensor, carry_in: Optional[torch.Tensor] = None,
     return C, total
 
 
-def carry_apply(U: torch.Tensor, C: torch.Tensor, chunk: int, hat_dtype: torch.dtype):
-    """q^, k^, v^ (BH,T,d) each, in hat_dtype."""
+def vt_stride(T: int) -> int:
+    return int(_lib.load().hoa_vt_stride(T))
+
+
+def carry_apply(U: torch.Tensor, C: torch.Tensor, chunk: int, hat_dtype: torch.dtype,
+                v_transposed: bool = False):
+    """q^, k^ (BH,T,d) and v^ (BH,T,d), or v^T (BH,d,vt_stride(T)) if v_transposed."""
     _need_cuda(U, C)
     BH, T, _, d = U.shape
-    outs = [torch.empty(BH, T, d, dtype=hat_dtype, device=U.device) for _ in range(3)]
-    _lib.call("hoa_carry_apply", _ptr(U), _ptr(C), *(_ptr(o) for o in outs), _dtype_code(hat_dtype),
-              BH, T, d, int(chunk), _stream(U.device))
-    return tuple(outs)
+    dev = U.device
+    qh = torch.empty(BH, T, d, dtype=hat_dtype, device=dev)
+    kh = torch.empty(BH, T, d, dtype=hat_dtype, device=dev)
+    vs = vt_stride(T) if v_transposed else 0
+    vh = (torch.empty(BH, d, vs, dtype=hat_dtype, device=dev) if v_transposed
+          else torch.empty(BH, T, d, dtype=hat_dtype, device=dev))
+    _lib.call("hoa_carry_apply", _ptr(U), _ptr(C), _ptr(qh), _ptr(kh), _ptr(vh),
+              _dtype_code(hat_dtype), vs, BH, T, d, int(chunk), _stream(dev))
+    return qh, kh, vh
 
 
-def attn_fwd(qh: torch.Tensor, kh: torch.Tensor, vh: torch.Tensor, R: torch.Tensor,
-             C: torch.Tensor, chunk: int, B: int, H: int, softmax_scale: float,
-             out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
-    """Kernels (3)+(4): causal attention + out_t = R_t C_k o_t -> (B,T,H*d)."""
-    _need_cuda(qh, kh, vh, R, C)
+def attn_fwd(qh: torch.Tensor, kh: torch.Tensor, vh: torch.Tensor,
+             softmax_scale: float) -> torch.Tensor:
+    """Kernel (3), fp32 SIMT path: o = softmax(q^ k^T * scale, causal) v^ -> (BH,T,d) fp32."""
+    _need_cuda(qh, kh, vh)
     BH, T, d = qh.shape
-    out_dtype = out_dtype or qh.dtype
-    out = torch.empty(B, T, H * d, dtype=out_dtype, device=qh.device)
-    _lib.call("hoa_attn_fwd", _ptr(qh), _ptr(kh), _ptr(vh), _dtype_code(qh.dtype), _ptr(R), _ptr(C),
-              int(chunk), _ptr(out), _dtype_code(out_dtype), float(softmax_scale), B, H, T, d,
-              _stream(qh.device))
+    o = torch.empty(BH, T, d, dtype=torch.float32, device=qh.device)
+    _lib.call("hoa_attn_fwd", _ptr(qh), _ptr(kh), _ptr(vh), _dtype_code(qh.dtype), _ptr(o),
+              float(softmax_scale), BH, T, d, _stream(qh.device))
+    return o
+
+
+def attn_tc_fwd(qh: torch.Tensor, kh: torch.Tensor, vhT: torch.Tensor, softmax_scale: float,
+                status: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Kernel (3), tcgen05 bf16 path (v^ transposed) -> o (BH,T,d) fp32."""
+    _need_cuda(qh, kh, vhT)
+    BH, T, d = qh.shape
+    if qh.dtype != torch.bfloat16:
+        raise NotImplementedError("the tensor-core attention takes bf16 q^/k^/v^")
+    o = torch.empty(BH, T, d, dtype=torch.float32, device=qh.device)
+    _lib.call("hoa_attn_tc_fwd", _ptr(qh), _ptr(kh), _ptr(vhT), _ptr(o), _ptr(status),
+              float(softmax_scale), BH, T, d, _stream(qh.device))
+    return o
+
+
+def out_transport(o: torch.Tensor, R: torch.Tensor, C: torch.Tensor, chunk: int, B: int, H: int,
+                  out_dtype: torch.dtype) -> torch.Tensor:
+    """Kernel (4): out_t = R_t C_k o_t -> (B,T,H*d) in out_dtype."""
+    _need_cuda(o, R, C)
+    BH, T, d = o.shape
+    out = torch.empty(B, T, H * d, dtype=out_dtype, device=o.device)
+    _lib.call("hoa_out_transport", _ptr(o), _ptr(R), _ptr(C), int(chunk), _ptr(out),
+              _dtype_code(out_dtype), B, H, T, d, _stream(o.device))
     return out
+
+
+def uses_tensor_cores(hat_dtype: torch.dtype, d: int) -> bool:
+    """Same rule as the library: bf16 hats with d % 8 == 0 and d <= 128."""
+    return hat_dtype == torch.bfloat16 and d % 8 == 0 and d <= 128
+
+
+def core_stages(a_all, qkv, n_heads, edge_scale, softmax_scale, out_dtype, hat_dtype, chunk):
+    """The core region as separate stage calls (same kernels as core_forward)."""
+    B, T, threeD = qkv.shape
+    H = n_heads
+    d = threeD // 3 // H
+    R, U, M = link_local(a_all, qkv, H, edge_scale, chunk)
+    C, _ = carry_scan(M)
+    tc = uses_tensor_cores(hat_dtype, d)
+    qh, kh, vh = carry_apply(U, C, chunk, hat_dtype, v_transposed=tc)
+    o = attn_tc_fwd(qh, kh, vh, softmax_scale) if tc else attn_fwd(qh, kh, vh, softmax_scale)
+    return out_transport(o, R, C, chunk, B, H, out_dtype)

@@ -53,7 +53,9 @@ const char* hoa_status_string(int status);
  * device's SM count.  Returns a multiple of 16 in [16, T] (or T when T < 16). */
 int hoa_plan_chunk(int B, int H, int T, int d, int num_sms);
 
-/* Bytes of scratch hoa_core_forward needs. */
+/* Bytes of scratch hoa_core_forward needs.  The first 4 bytes of the
+ * workspace receive a device status word (0, or HOA_ERR_TIMEOUT when a
+ * bounded device-side wait gave up); read it after the stream completes. */
 size_t hoa_core_workspace_bytes(int B, int H, int T, int d, int chunk, int hat_dtype);
 
 /*
@@ -64,12 +66,13 @@ size_t hoa_core_workspace_bytes(int B, int H, int T, int d, int chunk, int hat_d
  *   core/attention_fast_chunked.py:119-171 causal fold and out_i = P_i o_i
  * (kernel/attention_kernel.py:215-216 `_geometry` + `HoloAttnFn.apply`).
  * a_dtype / qkv_dtype / out_dtype: HOA_F32 or HOA_BF16.  hat_dtype is the
- * dtype of the transported q^/k^/v^ fed to attention (HOA_BF16 for bf16
- * activations, HOA_F32 for fp32).  `carry_in` (nullable, (B*H, d, d) fp32)
- * is P at the first position (a previous shard's product; NULL = identity);
- * `total_out` (nullable, (B*H, d, d)) receives the product through the last
- * edge t = T-1 (for a full sequence that edge is the closing edge, and
- * total_out is the holonomy G_close P_{T-1}, core/attention_fast_chunked.py:95).
+ * dtype of the transported q^/k^/v^ fed to attention: HOA_BF16 runs the
+ * tcgen05 tensor-core attention (d % 8 == 0, d <= 128), HOA_F32 the fp32 SIMT
+ * attention.  `carry_in` (nullable, (B*H, d, d) fp32) is P at the first
+ * position (a previous shard's product; NULL = identity); `total_out`
+ * (nullable, (B*H, d, d)) receives the product through the last edge
+ * t = T-1 (for a full sequence that edge is the closing edge, and total_out
+ * is the holonomy G_close P_{T-1}, core/attention_fast_chunked.py:95).
  */
 int hoa_core_forward(const void* a_all, int a_dtype, float edge_scale,
                      const void* qkv, int qkv_dtype,
@@ -103,23 +106,44 @@ int hoa_carry_scan(const float* M, const float* carry_in, float* C, float* total
                    int BH, int K, int d, void* stream);
 
 /*
- * Kernel (2), transport: q^_t = C_k^T U_q[t] (likewise k, v), written as
- * (B*H, T, d) in hat_dtype.  Completes core/attention_fast_chunked.py:108-110.
+ * Kernel (2), transport: q^_t = C_k^T U_q[t] (likewise k, v) in hat_dtype.
+ * q^, k^: (B*H, T, d).  v^: (B*H, T, d) when vt_stride == 0, else transposed
+ * as (B*H, d, vt_stride) with vt_stride = hoa_vt_stride(T) (the layout
+ * hoa_attn_tc_fwd reads).  Completes core/attention_fast_chunked.py:108-110.
  */
 int hoa_carry_apply(const float* U, const float* C, void* qh, void* kh, void* vh,
-                    int hat_dtype, int BH, int T, int d, int chunk, void* stream);
+                    int hat_dtype, int vt_stride, int BH, int T, int d, int chunk,
+                    void* stream);
+
+/* Row stride (elements) of the transposed v^ buffer: T rounded up to 8. */
+int hoa_vt_stride(int T);
 
 /*
- * Kernels (3)+(4): causal online-softmax attention on q^/k^/v^ (B*H, T, d)
- * with fp32 accumulation, then out_t = R_t (C_{t/chunk} o_t) written to
- * out (B, T, H, d) in out_dtype.
- * Replaces core/attention_fast_chunked.py:119-171 (kernel/attention_kernel.py:122-134
+ * Kernel (3), fp32 path: causal online-softmax attention on q^/k^/v^
+ * (B*H, T, d) in fp32 (or bf16) with every product in fp32; writes the
+ * normalised o = softmax(q^ k^T * scale) v^ as (B*H, T, d) fp32.
+ * Replaces core/attention_fast_chunked.py:119-168 (kernel/attention_kernel.py:122-134
  * run_fwd_kernel) for the causal tril mask.
  */
 int hoa_attn_fwd(const void* qh, const void* kh, const void* vh, int hat_dtype,
-                 const float* R, const float* C, int chunk,
-                 void* out, int out_dtype, float softmax_scale,
-                 int B, int H, int T, int d, void* stream);
+                 float* o, float softmax_scale, int BH, int T, int d, void* stream);
+
+/*
+ * Kernel (3), bf16 path on tcgen05/TMEM: same contract as hoa_attn_fwd with
+ * bf16 q^, k^ (B*H, T, d) and v^ transposed (B*H, d, hoa_vt_stride(T));
+ * fp32 accumulation.  d % 8 == 0, d <= 128.  `status` (nullable device int)
+ * receives HOA_ERR_TIMEOUT if a bounded wait gave up.
+ */
+int hoa_attn_tc_fwd(const void* qh, const void* kh, const void* vhT, float* o, int* status,
+                    float softmax_scale, int BH, int T, int d, void* stream);
+
+/*
+ * Kernel (4): inverse transport out_t = R_t (C_{t/chunk} o_t), written to
+ * out (B, T, H, d) in out_dtype — the input of the `out` projection.
+ * Replaces core/attention_fast_chunked.py:171.
+ */
+int hoa_out_transport(const float* o, const float* R, const float* C, int chunk,
+                      void* out, int out_dtype, int B, int H, int T, int d, void* stream);
 
 #ifdef __cplusplus
 }

@@ -35,7 +35,12 @@ def core_forward(a_all: torch.Tensor, q: torch.Tensor, k: torch.Tensor, v: torch
     d = q.shape[-1]
     a_all = a_all * edge_scale
     q, k, v = q.to(dt), k.to(dt), v.to(dt)
-    G = torch.matrix_exp(skew_from_vec(a_all[:, :, :-1], d))
+    # expm in batches of at most 4096 matrices: keeps every library call small
+    a_adj = a_all[:, :, :-1].reshape(-1, m)
+    G = torch.empty(a_adj.shape[0], d, d, dtype=dt, device=a_all.device)
+    for i0 in range(0, a_adj.shape[0], 4096):
+        G[i0:i0 + 4096] = torch.matrix_exp(skew_from_vec(a_adj[i0:i0 + 4096], d))
+    G = G.view(B, H, L - 1, d, d)
     P = torch.empty(B, H, L, d, d, dtype=dt, device=a_all.device)
     Pt = torch.eye(d, dtype=dt, device=a_all.device).expand(B, H, d, d).clone()
     P[:, :, 0] = Pt

@@ -1,0 +1,116 @@
+"""Stage-level GPU tests: each kernel of the core region against a float64 torch reference.
+
+Kernel (3) has two variants: fp32 SIMT (hoa_attn_fwd) and bf16 tcgen05
+(hoa_attn_tc_fwd, v^ transposed); kernel (4) is hoa_out_transport.
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from holonomyawareattention_b200 import ops
+from oracle.holonomy_oracle import rel_l2
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def causal_ref(qh, kh, vh, scale):
+    q, k, v = (t.double() for t in (qh, kh, vh))
+    T = q.shape[1]
+    s = (q @ k.transpose(1, 2)) * scale
+    s = s.masked_fill(~torch.tril(torch.ones(T, T, dtype=torch.bool, device=q.device)), float("-inf"))
+    return torch.softmax(s, -1) @ v
+
+
+@pytest.mark.parametrize("T", [1, 70, 150])
+@pytest.mark.parametrize("d", [8, 48, 96, 120])
+def test_attn_simt_fp32(T, d):
+    torch.manual_seed(T + d)
+    BH = 3
+    qh, kh, vh = (torch.randn(BH, T, d, device=DEV) for _ in range(3))
+    o = ops.attn_fwd(qh, kh, vh, 1 / math.sqrt(d))
+    assert rel_l2(o.cpu().numpy(), causal_ref(qh, kh, vh, 1 / math.sqrt(d)).cpu().numpy()) < 1e-6
+
+
+@pytest.mark.parametrize("T", [1, 100, 128, 129, 300])
+@pytest.mark.parametrize("d", [16, 48, 64, 96, 120, 128])
+def test_attn_tc_bf16(T, d):
+    """tcgen05 attention vs float64 softmax on the same bf16 inputs (P is rounded to bf16)."""
+    torch.manual_seed(1000 + T + d)
+    BH = 3
+    qh, kh, vh = (torch.randn(BH, T, d, device=DEV).to(torch.bfloat16) for _ in range(3))
+    vt = torch.zeros(BH, d, ops.vt_stride(T), dtype=torch.bfloat16, device=DEV)
+    vt[:, :, :T] = vh.transpose(1, 2)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    scale = 1 / math.sqrt(d)
+    o = ops.attn_tc_fwd(qh, kh, vt, scale, status)
+    ref = causal_ref(qh, kh, vh, scale)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    err = rel_l2(o.cpu().numpy(), ref.cpu().numpy())
+    assert err < 1e-2, err
+
+
+def test_attn_tc_large_scores():
+    """Peaked softmax (large logits) exercises the running-max correction."""
+    torch.manual_seed(7)
+    BH, T, d = 2, 384, 96
+    qh = (4 * torch.randn(BH, T, d, device=DEV)).to(torch.bfloat16)
+    kh = (4 * torch.randn(BH, T, d, device=DEV)).to(torch.bfloat16)
+    vh = torch.randn(BH, T, d, device=DEV).to(torch.bfloat16)
+    vt = torch.zeros(BH, d, ops.vt_stride(T), dtype=torch.bfloat16, device=DEV)
+    vt[:, :, :T] = vh.transpose(1, 2)
+    o = ops.attn_tc_fwd(qh, kh, vt, 1 / math.sqrt(d))
+    ref = causal_ref(qh, kh, vh, 1 / math.sqrt(d))
+    assert rel_l2(o.cpu().numpy(), ref.cpu().numpy()) < 1e-2
+
+
+@pytest.mark.parametrize("d", [8, 48, 96, 120])
+def test_out_transport(d):
+    torch.manual_seed(d)
+    B, H, T, chunk = 2, 3, 50, 16
+    K = (T + chunk - 1) // chunk
+    o = torch.randn(B * H, T, d, device=DEV)
+    R = torch.randn(B * H, T, d, d, device=DEV)
+    C = torch.randn(B * H, K, d, d, device=DEV)
+    for dt in (torch.float32, torch.bfloat16):
+        out = ops.out_transport(o, R, C, chunk, B, H, dt)
+        kidx = torch.arange(T, device=DEV) // chunk
+        w = torch.einsum("ntef,ntf->nte", C[:, kidx].double(), o.double())
+        ref = torch.einsum("ntef,ntf->nte", R.double(), w).view(B, H, T, d).transpose(1, 2).reshape(B, T, H * d)
+        tol = 1e-6 if dt == torch.float32 else 1e-2
+        assert rel_l2(out.float().cpu().numpy(), ref.cpu().numpy()) < tol
+
+
+def test_carry_apply_transposed_matches():
+    torch.manual_seed(3)
+    BH, T, d, chunk = 4, 77, 48, 16
+    K = (T + chunk - 1) // chunk
+    U = torch.randn(BH, T, 3, d, device=DEV)
+    C = torch.randn(BH, K, d, d, device=DEV)
+    q1, k1, v1 = ops.carry_apply(U, C, chunk, torch.bfloat16, v_transposed=False)
+    q2, k2, vt = ops.carry_apply(U, C, chunk, torch.bfloat16, v_transposed=True)
+    assert torch.equal(q1, q2) and torch.equal(k1, k2)
+    assert torch.equal(v1, vt[:, :, :T].transpose(1, 2))
+    kidx = torch.arange(T, device=DEV) // chunk
+    ref = torch.einsum("ntfe,ntf->nte", C[:, kidx].double(), U[:, :, 0].double())
+    assert rel_l2(q1.float().cpu().numpy(), ref.cpu().numpy()) < 1e-2
+    q3, _, _ = ops.carry_apply(U, C, chunk, torch.float32)
+    assert rel_l2(q3.cpu().numpy(), ref.cpu().numpy()) < 1e-6
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_stages_equal_core_forward(dtype):
+    """The one-call hoa_core_forward equals the stage-by-stage calls."""
+    torch.manual_seed(11)
+    B, T, H, d = 2, 90, 3, 48
+    m = d * (d - 1) // 2
+    a = (0.02 * torch.randn(B, T, H * m, device=DEV)).float()
+    qkv = torch.randn(B, T, 3 * H * d, device=DEV).to(dtype)
+    chunk = 32
+    y1 = ops.core_forward(a, qkv, H, 0.5, chunk=chunk)
+    y2 = ops.core_stages(a, qkv, H, 0.5, 1 / math.sqrt(d), dtype, dtype, chunk)
+    torch.cuda.synchronize()
+    assert torch.equal(y1, y2)

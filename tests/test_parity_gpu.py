@@ -119,20 +119,6 @@ def test_link_stage_geometry_vs_oracle():
         assert np.abs(np.swapaxes(P, -1, -2) @ P - I).max() < 1e-5
 
 
-def test_attention_stage_vs_torch():
-    """Kernel (3)+(4) alone: identity rotations reduce it to causal attention."""
-    torch.manual_seed(0)
-    B, H, T, d = 2, 3, 150, 96
-    qh, kh, vh = (torch.randn(B * H, T, d, device=DEV) for _ in range(3))
-    R = torch.eye(d, device=DEV).expand(B * H, T, d, d).contiguous()
-    C = torch.eye(d, device=DEV).expand(B * H, 1, d, d).contiguous()
-    out = ops.attn_fwd(qh, kh, vh, R, C, T, B, H, 1 / math.sqrt(d), torch.float32)
-    s = (qh @ kh.transpose(1, 2)) / math.sqrt(d)
-    s = s.masked_fill(~torch.tril(torch.ones(T, T, dtype=torch.bool, device=DEV)), float("-inf"))
-    ref = (torch.softmax(s.double(), -1) @ vh.double()).view(B, H, T, d).transpose(1, 2).reshape(B, T, H * d)
-    assert O.rel_l2(out.cpu().numpy(), ref.cpu().numpy()) < 1e-6
-
-
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_config2_full_size(dtype):
     """B=64, T=512, d_model=192, H=4 against the torch restatement (fp32)."""
