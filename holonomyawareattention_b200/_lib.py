@@ -39,6 +39,9 @@ SIGNATURES = {
                                 c_int, c_int, c_void_p]),
     "hoa_out_transport": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_int,
                                   c_int, c_int, c_int, c_void_p]),
+    "hoa_core_forward_noalloc": (c_int, [c_void_p, c_int, c_float, c_void_p, c_int, c_void_p, c_int,
+                                         c_int, c_float, c_void_p, c_void_p, c_int, c_int, c_int,
+                                         c_int, c_int, c_void_p]),
 }
 
 _lock = threading.Lock()

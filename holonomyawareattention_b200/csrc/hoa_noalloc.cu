@@ -1,0 +1,65 @@
+// hoa_core_forward_noalloc: the core region for callers that cannot allocate
+// device memory at call time (for example an inference-engine plugin whose
+// enqueue callback must not call cudaMalloc, or a process whose device memory
+// is reserved in full by another allocator).  It runs exactly the kernels of
+// hoa_core_forward; only the scratch differs: it lives in a static device
+// array compiled into this file, so nothing is allocated per call.
+//
+// Limits and sharing, stated for users:
+//   * the array holds HOA_NOALLOC_SCRATCH_BYTES (16 MiB); every GPU on which
+//     this part of the library is loaded keeps it until the process exits;
+//   * problems that need more scratch (hoa_core_workspace_bytes) are rejected
+//     with HOA_ERR_WORKSPACE before any GPU work is enqueued;
+//   * all calls on a device share the one array and it keeps the last call's
+//     contents; the status word at its start is cleared by every call, and
+//     every other byte a call reads was written earlier in the same call.
+//     Calls that overlap on the GPU (different streams, or several host
+//     threads) race on the array: serialise them.
+#include <mutex>
+
+#include "hoa_common.cuh"
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[HOA_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on the current device.  Host code may
+// not use the array's name as a device pointer (it names a host-side stand-in),
+// so the address is looked up once per device with that device current, and
+// cached.
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return HOA_ERR_LAUNCH;
+  if (dev < 0 || dev >= kMaxDevices) return HOA_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr)
+      return HOA_ERR_LAUNCH;
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return HOA_OK;
+}
+}  // namespace
+
+extern "C" int hoa_core_forward_noalloc(const void* a_all, int a_dtype, float edge_scale,
+                                        const void* qkv, int qkv_dtype, void* out, int out_dtype,
+                                        int hat_dtype, float softmax_scale, const float* carry_in,
+                                        float* total_out, int B, int H, int T, int d, int chunk,
+                                        void* stream) {
+  if (!a_all || !qkv || !out || B < 1 || H < 1 || T < 1 || d < 1 || chunk < 1)
+    return HOA_ERR_INVALID_ARG;
+  const size_t need = hoa_core_workspace_bytes(B, H, T, d, chunk, hat_dtype);
+  if (need == 0) return HOA_ERR_INVALID_ARG;
+  if (need > (size_t)HOA_NOALLOC_SCRATCH_BYTES) return HOA_ERR_WORKSPACE;
+  void* scratch = nullptr;
+  const int st = noalloc_scratch(&scratch);
+  if (st != HOA_OK) return st;
+  return hoa_core_forward(a_all, a_dtype, edge_scale, qkv, qkv_dtype, out, out_dtype, hat_dtype,
+                          softmax_scale, carry_in, total_out, B, H, T, d, chunk, scratch,
+                          (size_t)HOA_NOALLOC_SCRATCH_BYTES, stream);
+}

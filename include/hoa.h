@@ -145,6 +145,32 @@ int hoa_attn_tc_fwd(const void* qh, const void* kh, const void* vhT, float* o, i
 int hoa_out_transport(const float* o, const float* R, const float* C, int chunk,
                       void* out, int out_dtype, int B, int H, int T, int d, void* stream);
 
+/* Size of the static scratch behind hoa_core_forward_noalloc: 16 MiB. */
+#define HOA_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
+
+/*
+ * hoa_core_forward_noalloc — no counterpart in the reference.  Same
+ * computation and arguments as hoa_core_forward minus the workspace, for
+ * callers that cannot allocate device memory when they call in (for example
+ * an inference-engine plugin whose enqueue callback must not call cudaMalloc,
+ * or a process whose device memory is reserved in full by another allocator).
+ * Its scratch is a static device array of HOA_NOALLOC_SCRATCH_BYTES inside
+ * the library, which every GPU that loads it keeps until the process exits;
+ * nothing is allocated per call.  Problems whose hoa_core_workspace_bytes
+ * exceeds that size return HOA_ERR_WORKSPACE without enqueuing work.
+ * It runs on the current device, and `stream` must belong to that device.
+ * The first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress) and caches it, so make that first call before any
+ * stream capture.  All calls share the array and it keeps the last call's
+ * contents: calls that overlap on the GPU (other streams, other host
+ * threads) race on it, so serialise them.
+ */
+int hoa_core_forward_noalloc(const void* a_all, int a_dtype, float edge_scale,
+                             const void* qkv, int qkv_dtype,
+                             void* out, int out_dtype, int hat_dtype, float softmax_scale,
+                             const float* carry_in, float* total_out,
+                             int B, int H, int T, int d, int chunk, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
