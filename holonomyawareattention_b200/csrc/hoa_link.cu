@@ -473,15 +473,26 @@ extern "C" int hoa_plan_chunk(int B, int H, int T, int d, int num_sms) {
   return (int)chunk;
 }
 
-extern "C" int hoa_link_local(const void* a_all, int a_dtype, float edge_scale, const void* qkv,
-                              int qkv_dtype, float* R, float* U, float* M, int B, int H, int T,
-                              int d, int chunk, void* stream) {
+namespace hoa {
+int link_local_tc(const void* a_all, int a_dtype, float edge_scale, const void* qkv,
+                  int qkv_dtype, float* R, float* U, float* M, int* status, int B, int H, int T,
+                  int d, int chunk, cudaStream_t s);
+}
+
+// The tensor-core kernel serves d in {32, 48, 64, 96} with fp32 generators; every
+// other shape runs the SIMT kernel.  Both compute the same fp32-accurate result.
+static int link_local_dispatch(const void* a_all, int a_dtype, float edge_scale, const void* qkv,
+                               int qkv_dtype, float* R, float* U, float* M, int* status, int B,
+                               int H, int T, int d, int chunk, void* stream) {
   if (!a_all || !qkv || !R || !U || !M || B < 1 || H < 1 || T < 1 || d < 1 || chunk < 1)
     return HOA_ERR_INVALID_ARG;
   if (!valid_dtype(a_dtype) || !valid_dtype(qkv_dtype)) return HOA_ERR_UNSUPPORTED;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int tc = link_local_tc(a_all, a_dtype, edge_scale, qkv, qkv_dtype, R, U, M, status, B, H,
+                               T, d, chunk, s);
+  if (tc != HOA_ERR_UNSUPPORTED) return tc;
   LinkArgs a{a_all, a_dtype, edge_scale, qkv, qkv_dtype, R, U, M, B, H, T, d, chunk,
              ceil_div(T, chunk)};
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   switch (padded_dim(d)) {
     case 8: return launch_link_local<8>(a, s);
     case 16: return launch_link_local<16>(a, s);
@@ -492,6 +503,13 @@ extern "C" int hoa_link_local(const void* a_all, int a_dtype, float edge_scale, 
     case 120: return launch_link_local<120>(a, s);
     default: return HOA_ERR_UNSUPPORTED;
   }
+}
+
+extern "C" int hoa_link_local(const void* a_all, int a_dtype, float edge_scale, const void* qkv,
+                              int qkv_dtype, float* R, float* U, float* M, int B, int H, int T,
+                              int d, int chunk, void* stream) {
+  return link_local_dispatch(a_all, a_dtype, edge_scale, qkv, qkv_dtype, R, U, M, nullptr, B, H,
+                             T, d, chunk, stream);
 }
 
 extern "C" int hoa_carry_scan(const float* M, const float* carry_in, float* C, float* total_out,
@@ -598,8 +616,8 @@ extern "C" int hoa_core_forward(const void* a_all, int a_dtype, float edge_scale
   const int K = ceil_div(T, chunk);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (cudaMemsetAsync(status, 0, sizeof(int), s) != cudaSuccess) return HOA_ERR_LAUNCH;
-  int st = hoa_link_local(a_all, a_dtype, edge_scale, qkv, qkv_dtype, R, U, M, B, H, T, d, chunk,
-                          stream);
+  int st = link_local_dispatch(a_all, a_dtype, edge_scale, qkv, qkv_dtype, R, U, M, status, B, H,
+                               T, d, chunk, stream);
   if (st != HOA_OK) return st;
   st = hoa_carry_scan(M, carry_in, C, total_out, B * H, K, d, stream);
   if (st != HOA_OK) return st;

@@ -1,0 +1,538 @@
+// Kernels (1)+(2) on tcgen05: link rotations G_t = expm(skew(edge_scale a_t))
+// and the local prefix products R_{t+1} = G_t R_t, fp32-accurate through
+// 3xTF32 (x = hi + lo, both tf32; X Y ~ Xhi Yhi + Xhi Ylo + Xlo Yhi).
+//
+// Same contract and reference semantics as link_local_kernel in hoa_link.cu
+// (core/utils.py:4-52, core/attention_fast_chunked.py:77, 86-94, 108-110);
+// this variant serves d in {32, 48, 64, 96} with fp32 generators.
+//
+// One CTA of 4 warps per (chain, chunk); thread r owns row r of every d x d
+// matrix (TMEM lane r = row r of every accumulator).  Every product D = X Y
+// takes X as rows (K-major) and Y as the rows of Y^T (K-major B operand), in
+// the 128B-swizzled layout; the matrices are polynomials in the skew A, so
+// p(A)^T = p(-A) gives most transposes for free:
+//   P1  D1 = A A^T = -A^2            X = Y^T = A rows (one buffer)
+//   P2  D2 = A2s T1 = A4             Y^T = T1^T = -x1 As + x2 A2s  (As = A 2^-s, A2s = A^2 4^-s)
+//   P3  D2 = L F                     L = x3 A2s + A4, F = x5 As + x6 A2s + x7 A4 (= Rf - x4 I);
+//                                    F^T needs A4^T, read back through a padded shared-memory transpose
+//       N  = G - I = As + (y2 + x3 x4) A2s + x4 A4 + D2      (fp32, CUDA cores)
+//       s squarings: N <- 2N + N N   (N^T by the same transpose)
+//   P4  D1 = R^T N^T                 A operand R^T (hi, lo) from TMEM, B = N rows
+//       R_{t+1}^T = R^T + D1         (fp32, CUDA cores; R^T kept exactly in TMEM)
+// Keeping the identity out of every tensor-core product makes the MMA's own
+// accumulation rounding scale with the small delta (|N| ~ |A|), not with |G R|.
+// The running product lives in TMEM as R^T (fp32, and tf32 hi/lo columns), the
+// A operand the next composition needs.  A double-buffered generator vector is
+// fetched by 1-D bulk TMA copies.
+#include "hoa_sm100.cuh"
+
+namespace hoa {
+using namespace sm100;
+
+constexpr int kLtThreads = 128;
+
+// T8 coefficients (derivation in hoa_link.cu).
+__constant__ float kT8tc[8] = {
+    0.059249617736388274f, 0.014812404434097069f, 0.36450763864714936f, 1.0f,
+    0.29469080354241967f,  0.025771599210148963f, 0.11303901220301756f, 0.13549236135285064f,
+};
+constexpr float kTheta8tc = 0.6f;
+
+template <int DP>
+struct LtLayout {
+  static constexpr int NSLAB = (DP + 31) / 32;
+  static constexpr int kSlab = DP * 128;               // DP rows of 128 bytes
+  static constexpr int kMat = NSLAB * kSlab;           // one split (hi or lo) of one matrix
+  // An A operand is read as 128 rows (M = 128), i.e. 128 - DP rows past the
+  // end of its last slab; the transpose scratch that follows covers that.
+  static constexpr int offYhi = 0;
+  static constexpr int offYlo = kMat;
+  static constexpr int offXhi = 2 * kMat;
+  static constexpr int offXlo = 3 * kMat;
+  static constexpr int offXT = 4 * kMat;                 // fp32 [DP][DP+1] transpose scratch
+  static constexpr int kXTbytes = DP * (DP + 1) * 4;
+  static constexpr int kXend = offXlo + (NSLAB - 1) * kSlab + 128 * 128;
+  static constexpr int kEnd0 = offXT + kXTbytes > kXend ? offXT + kXTbytes : kXend;
+  static constexpr int offStage = (kEnd0 + 1023) / 1024 * 1024;
+  static constexpr int kStage = ((DP * (DP - 1) / 2) * 4 + 127) / 128 * 128;
+  static constexpr int offVec = offStage + 2 * kStage;
+  static constexpr int offRed = offVec + 3 * DP * 4;
+  static constexpr int offBar = offRed + 64;
+  static constexpr int kBytes = offBar + 64;
+  // TMEM: R^T hi, R^T lo, R^T fp32, D1, D2 (DP columns each), rounded up to a power of two.
+  static constexpr uint32_t kTmemCols = 5 * DP <= 128 ? 128 : (5 * DP <= 256 ? 256 : 512);
+  // Request enough shared memory that no more CTAs share an SM than its 512
+  // TMEM columns can serve (an allocation would otherwise wait for a peer).
+  static constexpr int kMaxCtas = 512 / kTmemCols;
+  static constexpr int kMinAlloc = 233472 / (kMaxCtas + 1);
+  static constexpr int kAlloc = (kBytes + 1024 > kMinAlloc) ? kBytes + 1024 : kMinAlloc;
+  static_assert(kSlab % 1024 == 0, "slabs must stay 1024-aligned");
+  static_assert(kAlloc <= 232448, "shared memory budget");
+};
+
+struct LinkTcArgs {
+  const float* a; float edge_scale;
+  const void* qkv; int qkv_dtype;
+  float* R; float* U; float* M;
+  int* status;
+  int B, H, T, chunk, K;
+};
+
+// Row r, columns [c0, c0+16) of A = skew(edge_scale * a) from the staged vector.
+// S_i = i (2d - i - 1) / 2 is the offset of row i's strict upper triangle.
+template <int DP>
+HOA_DEVICE void skew_row16(const float* __restrict__ av, float es, int r, int c0, float (&v)[16]) {
+  const int Sr = r * (2 * DP - r - 1) / 2;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const int c = c0 + i;
+    float x = 0.f;
+    if (c > r) x = __fmul_rn(av[Sr + c - r - 1], es);
+    else if (c < r) x = -__fmul_rn(av[c * (2 * DP - c - 1) / 2 + r - c - 1], es);
+    v[i] = x;
+  }
+}
+
+// Write 16 values of row `row`, columns [c0, c0+16), as tf32 hi and lo into
+// two swizzled operand buffers (slab = c0 / 32).
+template <int DP>
+HOA_DEVICE void put_row16(uint8_t* hi_buf, uint8_t* lo_buf, int row, int c0, const float (&v)[16]) {
+  using L = LtLayout<DP>;
+  const int slab = c0 >> 5;
+  const int ch0 = (c0 & 31) >> 2;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    float h[4], l[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      h[i] = to_tf32(v[4 * q + i]);
+      l[i] = to_tf32(v[4 * q + i] - h[i]);
+    }
+    const uint32_t off = slab * L::kSlab + sw128_offset(row, ch0 + q);
+    *reinterpret_cast<float4*>(hi_buf + off) = make_float4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<float4*>(lo_buf + off) = make_float4(l[0], l[1], l[2], l[3]);
+  }
+}
+
+// 3-pass SS product D = X Y with X given as rows and Y as the rows of Y^T
+// (both K-major, 128B-swizzled).
+template <int DP>
+HOA_DEVICE void issue_ss(uint32_t d_tmem, uint32_t xhi, uint32_t xlo, uint32_t yhi, uint32_t ylo) {
+  using L = LtLayout<DP>;
+  constexpr uint32_t id = make_idesc(kFmtTF32, 128, DP);
+  const uint32_t xs[3] = {xhi, xhi, xlo};
+  const uint32_t ys[3] = {yhi, ylo, yhi};
+#pragma unroll
+  for (int ps = 0; ps < 3; ++ps)
+#pragma unroll
+    for (int kk = 0; kk < DP / 8; ++kk) {
+      const uint32_t off = (kk >> 2) * L::kSlab + (kk & 3) * 32;
+      mma_tf32(d_tmem, desc_sw128(xs[ps] + off), desc_sw128(ys[ps] + off), id, (ps | kk) ? 1u : 0u);
+    }
+}
+
+// 3-pass TS product D = A B^T: A from TMEM (hi, lo columns), B rows K-major in shared memory.
+template <int DP>
+HOA_DEVICE void issue_ts(uint32_t d_tmem, uint32_t ahi, uint32_t alo, uint32_t bhi, uint32_t blo) {
+  using L = LtLayout<DP>;
+  constexpr uint32_t id = make_idesc(kFmtTF32, 128, DP, false);
+  const uint32_t as[3] = {ahi, ahi, alo};
+  const uint32_t bs[3] = {bhi, blo, bhi};
+#pragma unroll
+  for (int ps = 0; ps < 3; ++ps)
+#pragma unroll
+    for (int kk = 0; kk < DP / 8; ++kk) {
+      const uint32_t ba = bs[ps] + (kk >> 2) * L::kSlab + (kk & 3) * 32;
+      mma_tf32_ts(d_tmem, as[ps] + kk * 8, desc_sw128(ba), id, (ps | kk) ? 1u : 0u);
+    }
+}
+
+template <int DP>
+__global__ void __launch_bounds__(kLtThreads, 1) link_tc_kernel(LinkTcArgs p) {
+  using L = LtLayout<DP>;
+  constexpr int NC = DP / 16;            // 16-column chunks of a row
+  constexpr int m = DP * (DP - 1) / 2;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                           ~static_cast<uintptr_t>(1023));
+  uint8_t* Yhi = sm + L::offYhi;
+  uint8_t* Ylo = sm + L::offYlo;
+  uint8_t* Xhi = sm + L::offXhi;
+  uint8_t* Xlo = sm + L::offXlo;
+  float* XT = reinterpret_cast<float*>(sm + L::offXT);
+  float* stage0 = reinterpret_cast<float*>(sm + L::offStage);
+  float* svec = reinterpret_cast<float*>(sm + L::offVec);
+  float* sred = reinterpret_cast<float*>(sm + L::offRed);
+  uint64_t* bar_mma = reinterpret_cast<uint64_t*>(sm + L::offBar);
+  uint64_t* bar_a = bar_mma + 1;                        // two: one per generator stage
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_a + 2);
+
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int r = tid;                                     // this thread's row
+  const bool row_ok = r < DP;
+  const int chain = blockIdx.x / p.K;
+  const int kc = blockIdx.x % p.K;
+  const int b = chain / p.H, h = chain % p.H;
+  const int t0 = kc * p.chunk;
+  const int t1 = min(t0 + p.chunk, p.T);
+  const float es = p.edge_scale;
+
+  if (tid == 0) {
+    mbar_init(bar_mma, 1);
+    mbar_init(&bar_a[0], 1);
+    mbar_init(&bar_a[1], 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, L::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+  const uint32_t lane = static_cast<uint32_t>(warp * 32) << 16;
+  const uint32_t cRhi = tbase, cRlo = tbase + DP, cD1 = tbase + 2 * DP, cD2 = tbase + 3 * DP,
+                 cRf = tbase + 4 * DP;
+  const uint32_t sXhi = smem_u32(Xhi), sXlo = smem_u32(Xlo), sYhi = smem_u32(Yhi),
+                 sYlo = smem_u32(Ylo);
+
+  auto gen_ptr = [&](int t) {
+    return p.a + (((long long)b * p.T + t) * p.H + h) * (long long)m;
+  };
+  auto load_vec = [&](int t) {     // q, k, v of position t into svec
+    const long long qb = (((long long)b * p.T + t) * p.H + h) * 3LL * DP;
+    for (int i = tid; i < 3 * DP; i += kLtThreads) svec[i] = load_elem(p.qkv, qb + i, p.qkv_dtype);
+  };
+
+  if (tid == 0) {
+    mbar_arrive_expect_tx(&bar_a[0], m * 4);
+    bulk_load(stage0, gen_ptr(t0), m * 4, &bar_a[0]);
+  }
+  // position t0: R = I, U = (q, k, v); R^T = I in TMEM (hi = I, lo = 0)
+  load_vec(t0);
+  __syncthreads();
+  {
+    const long long pos = (long long)chain * p.T + t0;
+    float* Rg = p.R + pos * DP * DP;
+    for (int i = tid; i < DP * DP; i += kLtThreads) Rg[i] = (i / DP == i % DP) ? 1.f : 0.f;
+    float* Ug = p.U + pos * 3 * DP;
+    for (int i = tid; i < 3 * DP; i += kLtThreads) Ug[i] = svec[i];
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      float v[16], z[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) { v[i] = (c * 16 + i == r) ? 1.f : 0.f; z[i] = 0.f; }
+      tmem_st16(cRhi + lane + c * 16, v);
+      tmem_st16(cRlo + lane + c * 16, z);
+      tmem_st16(cRf + lane + c * 16, v);
+    }
+    tmem_wait_st();
+  }
+
+  uint32_t ph_mma = 0, ph_a0 = 0, ph_a1 = 0;
+  bool bad = false;
+  const float x1 = kT8tc[0], x2 = kT8tc[1], x3 = kT8tc[2], x4 = kT8tc[3], x5 = kT8tc[4],
+              x6 = kT8tc[5], x7 = kT8tc[6], y2 = kT8tc[7];
+
+  for (int t = t0; t < t1; ++t) {
+    const int sidx = (t - t0) & 1;
+    float* av = stage0 + sidx * (L::kStage / 4);
+    if (__syncthreads_or(bad)) { bad = true; break; }
+    // prefetch the next edge's generator into the other stage (its readers are done)
+    if (tid == 0 && t + 1 < t1) {
+      fence_proxy_async_smem();
+      float* nxt = stage0 + (sidx ^ 1) * (L::kStage / 4);
+      mbar_arrive_expect_tx(&bar_a[sidx ^ 1], m * 4);
+      bulk_load(nxt, gen_ptr(t + 1), m * 4, &bar_a[sidx ^ 1]);
+    }
+    if (t + 1 < t1) load_vec(t + 1);
+    if (sidx == 0) { bad |= !mbar_wait(&bar_a[0], ph_a0); ph_a0 ^= 1; }
+    else { bad |= !mbar_wait(&bar_a[1], ph_a1); ph_a1 ^= 1; }
+
+    // ---- P1: A rows -> X; D1 = A A^T = -A^2 ---------------------------------
+    if (row_ok) {
+#pragma unroll
+      for (int c = 0; c < NC; ++c) {
+        float v[16];
+        skew_row16<DP>(av, es, r, c * 16, v);
+        put_row16<DP>(Xhi, Xlo, r, c * 16, v);
+      }
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (tid == 0 && !bad) {
+      issue_ss<DP>(cD1, sXhi, sXlo, sXhi, sXlo);
+      tc_commit(bar_mma);
+    }
+    bad |= !mbar_wait(bar_mma, ph_mma);
+    ph_mma ^= 1;
+    tc_fence_after();
+
+    // ---- theta^2 = ||A^2||_1 (A^2 symmetric: max row abs-sum) ---------------
+    float rs = 0.f;
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      float v[16];
+      tmem_ld16(cD1 + lane + c * 16, v);
+      tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 16; ++i) rs += fabsf(v[i]);
+    }
+    if (!row_ok) rs = 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) rs = fmaxf(rs, __shfl_xor_sync(0xffffffffu, rs, o));
+    if ((tid & 31) == 0) sred[warp] = rs;
+    __syncthreads();
+    int nsq = 0;
+    {
+      float theta = sqrtf(fmaxf(fmaxf(sred[0], sred[1]), fmaxf(sred[2], sred[3])));
+      while (theta > kTheta8tc && nsq < 64) { theta *= 0.5f; ++nsq; }
+    }
+    const float sa = ldexpf(1.f, -nsq);
+    const float sa2 = -ldexpf(1.f, -2 * nsq);    // A2s = -D1 * 4^-s
+
+    // ---- P2: X = A2s rows, Y^T = T1^T rows -----------------------------------
+    // (TMEM loads are warp-collective: every lane executes them, rows or not.)
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      float a2[16];
+      tmem_ld16(cD1 + lane + c * 16, a2);
+      tmem_wait_ld();
+      if (row_ok) {
+        float a[16], t1v[16];
+        skew_row16<DP>(av, es, r, c * 16, a);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          a2[i] *= sa2;
+          t1v[i] = x2 * a2[i] - x1 * (a[i] * sa);             // row of T1^T
+        }
+        put_row16<DP>(Xhi, Xlo, r, c * 16, a2);
+        put_row16<DP>(Yhi, Ylo, r, c * 16, t1v);
+      }
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (tid == 0 && !bad) {
+      issue_ss<DP>(cD2, sXhi, sXlo, sYhi, sYlo);
+      tc_commit(bar_mma);
+    }
+    bad |= !mbar_wait(bar_mma, ph_mma);
+    ph_mma ^= 1;
+    tc_fence_after();
+
+    // ---- A4 -> transpose scratch, so that each thread can read its row of A4^T
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      float a4[16];
+      tmem_ld16(cD2 + lane + c * 16, a4);
+      tmem_wait_ld();
+      if (row_ok) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) XT[r * (DP + 1) + c * 16 + i] = a4[i];
+      }
+    }
+    __syncthreads();
+
+    // ---- P3: X = L rows, Y^T = F^T rows; N0 = As + (y2 + x3 x4) A2s + x4 A4 -> D1
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      float a2[16], a4[16], a[16], lv[16], fv[16], n0[16];
+      tmem_ld16(cD1 + lane + c * 16, a2);
+      tmem_ld16(cD2 + lane + c * 16, a4);
+      tmem_wait_ld();
+      if (row_ok) {
+        skew_row16<DP>(av, es, r, c * 16, a);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int col = c * 16 + i;
+          const float a2s = a2[i] * sa2;
+          const float as = a[i] * sa;
+          const float a4t = XT[col * (DP + 1) + r];               // A4^T[r][col] = A4[col][r]
+          lv[i] = x3 * a2s + a4[i];
+          fv[i] = x6 * a2s + x7 * a4t - x5 * as;
+          n0[i] = as + (y2 + x3 * x4) * a2s + x4 * a4[i];
+        }
+        put_row16<DP>(Xhi, Xlo, r, c * 16, lv);
+        put_row16<DP>(Yhi, Ylo, r, c * 16, fv);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) n0[i] = 0.f;
+      }
+      tmem_st16(cD1 + lane + c * 16, n0);
+    }
+    tmem_wait_st();
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (tid == 0 && !bad) {
+      issue_ss<DP>(cD2, sXhi, sXlo, sYhi, sYlo);        // D2 = L F
+      tc_commit(bar_mma);
+    }
+    bad |= !mbar_wait(bar_mma, ph_mma);
+    ph_mma ^= 1;
+    tc_fence_after();
+
+    // ---- N = G - I = N0 + D2, then s squarings N <- 2N + N N; N rows -> Y -------
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      float n0[16], g[16];
+      tmem_ld16(cD1 + lane + c * 16, n0);
+      tmem_ld16(cD2 + lane + c * 16, g);
+      tmem_wait_ld();
+      if (row_ok) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) g[i] += n0[i];
+        if (nsq > 0) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) XT[r * (DP + 1) + c * 16 + i] = g[i];
+        } else {
+          put_row16<DP>(Yhi, Ylo, r, c * 16, g);
+        }
+      }
+    }
+    for (int sq = 0; sq < nsq; ++sq) {      // N <- 2N + N N: X = N rows, Y^T = N^T rows
+      __syncthreads();                       // N rows complete in the scratch
+      if (row_ok) {
+#pragma unroll
+        for (int c = 0; c < NC; ++c) {
+          float g[16], gt[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            g[i] = XT[r * (DP + 1) + c * 16 + i];
+            gt[i] = XT[(c * 16 + i) * (DP + 1) + r];
+          }
+          put_row16<DP>(Xhi, Xlo, r, c * 16, g);
+          put_row16<DP>(Yhi, Ylo, r, c * 16, gt);
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncthreads();
+      tc_fence_after();
+      if (tid == 0 && !bad) {
+        issue_ss<DP>(cD2, sXhi, sXlo, sYhi, sYlo);
+        tc_commit(bar_mma);
+      }
+      bad |= !mbar_wait(bar_mma, ph_mma);
+      ph_mma ^= 1;
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < NC; ++c) {
+        float g[16];
+        tmem_ld16(cD2 + lane + c * 16, g);
+        tmem_wait_ld();
+        if (row_ok) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) g[i] = fmaf(2.f, XT[r * (DP + 1) + c * 16 + i], g[i]);
+        }
+        __syncwarp();
+        if (row_ok) {
+          if (sq + 1 < nsq) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) XT[r * (DP + 1) + c * 16 + i] = g[i];
+          } else {
+            put_row16<DP>(Yhi, Ylo, r, c * 16, g);
+          }
+        }
+      }
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+
+    // ---- P4: D1 = R^T N^T ------------------------------------------------------
+    if (tid == 0 && !bad) {
+      issue_ts<DP>(cD1, cRhi, cRlo, sYhi, sYlo);
+      tc_commit(bar_mma);
+    }
+    bad |= !mbar_wait(bar_mma, ph_mma);
+    ph_mma ^= 1;
+    tc_fence_after();
+
+    // ---- R_{t+1}^T = R^T + D1: keep it in TMEM (fp32, hi, lo); write R_{t+1}
+    //      and U_{t+1}, or the chunk total after the chunk's last edge.
+    const bool last = (t + 1 == t1);
+    const long long pos1 = (long long)chain * p.T + t + 1;
+    float* Rg = last ? p.M + ((long long)chain * p.K + kc) * DP * DP : p.R + pos1 * DP * DP;
+    float u0 = 0.f, u1 = 0.f, u2 = 0.f;
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      float v[16], dv[16], hv[16], lv[16];
+      tmem_ld16(cRf + lane + c * 16, v);
+      tmem_ld16(cD1 + lane + c * 16, dv);
+      tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        v[i] += dv[i];
+        hv[i] = to_tf32(v[i]);
+        lv[i] = to_tf32(v[i] - hv[i]);
+      }
+      tmem_st16(cRf + lane + c * 16, v);
+      tmem_st16(cRhi + lane + c * 16, hv);
+      tmem_st16(cRlo + lane + c * 16, lv);
+      if (row_ok) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int k = c * 16 + i;                 // v[i] = R_{t+1}[k][r]
+          Rg[(long long)k * DP + r] = v[i];
+          if (!last) {
+            u0 = fmaf(v[i], svec[k], u0);
+            u1 = fmaf(v[i], svec[DP + k], u1);
+            u2 = fmaf(v[i], svec[2 * DP + k], u2);
+          }
+        }
+      }
+    }
+    if (row_ok && !last) {
+      float* Ug = p.U + pos1 * 3 * DP;
+      Ug[r] = u0;
+      Ug[DP + r] = u1;
+      Ug[2 * DP + r] = u2;
+    }
+    tmem_wait_st();
+    tc_fence_before();
+  }
+
+  bad = __syncthreads_or(bad);
+  if (bad && tid == 0 && p.status != nullptr) atomicExch(p.status, HOA_ERR_TIMEOUT);
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tbase, L::kTmemCols);
+}
+
+template <int DP>
+int launch_link_tc(const LinkTcArgs& a, cudaStream_t s) {
+  using L = LtLayout<DP>;
+  if (cudaFuncSetAttribute(link_tc_kernel<DP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           L::kAlloc) != cudaSuccess)
+    return HOA_ERR_LAUNCH;
+  const long long units = (long long)a.B * a.H * a.K;
+  link_tc_kernel<DP><<<(unsigned)units, kLtThreads, L::kAlloc, s>>>(a);
+  return launch_status();
+}
+
+// Entry used by hoa_link_local: returns HOA_ERR_UNSUPPORTED when this variant
+// does not serve the shape (the caller then runs the SIMT kernel).
+int link_local_tc(const void* a_all, int a_dtype, float edge_scale, const void* qkv,
+                  int qkv_dtype, float* R, float* U, float* M, int* status, int B, int H, int T,
+                  int d, int chunk, cudaStream_t s) {
+  if (a_dtype != HOA_F32 || (reinterpret_cast<uintptr_t>(a_all) & 15) != 0)
+    return HOA_ERR_UNSUPPORTED;
+  LinkTcArgs a{static_cast<const float*>(a_all), edge_scale, qkv, qkv_dtype, R, U, M, status,
+               B, H, T, chunk, ceil_div(T, chunk)};
+  switch (d) {
+    case 32: return launch_link_tc<32>(a, s);
+    case 48: return launch_link_tc<48>(a, s);
+    case 64: return launch_link_tc<64>(a, s);
+    case 96: return launch_link_tc<96>(a, s);
+    default: return HOA_ERR_UNSUPPORTED;
+  }
+}
+
+}  // namespace hoa

@@ -3,6 +3,9 @@
 //
 // Every wait is bounded: a wait that gives up returns false and the caller
 // records HOA_ERR_TIMEOUT and leaves its loop (the GPU stays usable).
+// tcgen05.ld / tcgen05.st / tcgen05.wait::* / tcgen05.alloc are warp-collective
+// (.sync.aligned): callers execute them in every lane of the warp, never
+// inside a lane-dependent branch.
 #pragma once
 
 #include <cuda.h>
@@ -44,13 +47,23 @@ HOA_DEVICE bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait on the phase with the given parity (each try_wait itself
-// blocks for a hardware-defined window, so the bound is seconds, not spins).
-constexpr uint32_t kMaxWaitTries = 1u << 22;
+HOA_DEVICE uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait on the phase with the given parity: gives up after ~2 s of
+// wall time (each try_wait may itself suspend for a hardware-defined window,
+// so the bound is on the clock, not on the number of tries).
+constexpr uint64_t kMaxWaitNs = 2000000000ull;
 HOA_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kMaxWaitTries; ++i)
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-  return false;
+    if (globaltimer_ns() - t0 > kMaxWaitNs) return false;
+  }
 }
 
 // ---- TMA ---------------------------------------------------------------------
@@ -59,6 +72,16 @@ HOA_DEVICE void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, in
       "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
+// 1-D bulk copy global -> shared (TMA engine), completion counted on `bar`.
+// Source and destination 16-byte aligned, size a multiple of 16.
+HOA_DEVICE void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
 
@@ -113,13 +136,24 @@ HOA_DEVICE void mma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32
       : "memory");
 }
 
+// D(tmem) (+)= A(tmem) * B(smem); tf32 operands (kind::tf32), fp32 accumulate.
+HOA_DEVICE void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Instruction descriptor (kind::f16 / kind::tf32): fp32 accumulator, K-major A and B.
 //   bits 4-5 D format (1 = f32), 7-9 A format, 10-12 B format (1 = bf16, 2 = tf32),
 //   15/16 A/B major (0 = K), 17-22 N >> 3, 24-28 M >> 4.
 constexpr uint32_t kFmtBF16 = 1, kFmtTF32 = 2;
-__host__ __device__ constexpr uint32_t make_idesc(uint32_t fmt, int M, int N) {
-  return (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(N >> 3) << 17) |
-         ((uint32_t)(M >> 4) << 24);
+__host__ __device__ constexpr uint32_t make_idesc(uint32_t fmt, int M, int N, bool b_mn_major = false) {
+  return (1u << 4) | (fmt << 7) | (fmt << 10) | ((b_mn_major ? 1u : 0u) << 16) |
+         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
 // Shared-memory matrix descriptor, K-major operand in the 128-byte swizzled
@@ -131,6 +165,18 @@ __host__ __device__ constexpr uint32_t make_idesc(uint32_t fmt, int M, int N) {
 HOA_DEVICE uint64_t desc_sw128(uint32_t smem_addr) {
   uint64_t d = (uint64_t)((smem_addr >> 4) & 0x3FFFu);
   d |= (uint64_t)1u << 16;
+  d |= (uint64_t)(1024u >> 4) << 32;
+  d |= (uint64_t)1u << 46;
+  d |= (uint64_t)2u << 61;
+  return d;
+}
+
+// MN-major operand in the 128-byte swizzled canonical layout: 128-byte rows
+// along MN (32 tf32 / 64 bf16 per row) stacked along K, 8-row K groups 1024
+// bytes apart (SBO), MN slabs of 128 bytes `slab_bytes` apart (LBO).
+HOA_DEVICE uint64_t desc_sw128_mn(uint32_t smem_addr, uint32_t slab_bytes) {
+  uint64_t d = (uint64_t)((smem_addr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((slab_bytes >> 4) & 0x3FFFu) << 16;
   d |= (uint64_t)(1024u >> 4) << 32;
   d |= (uint64_t)1u << 46;
   d |= (uint64_t)2u << 61;
@@ -176,7 +222,52 @@ HOA_DEVICE void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 8 consecutive TMEM columns of this thread's lane (32x32b shape, x8).
+HOA_DEVICE void tmem_ld8(uint32_t taddr, float (&v)[8]) {
+  uint32_t r[8];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                 "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr)
+               : "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 HOA_DEVICE void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Store 8 consecutive TMEM columns of this thread's lane (32x32b shape, x8).
+HOA_DEVICE void tmem_st8(uint32_t taddr, const float (&v)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(
+                   taddr),
+               "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+               "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+               "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7]))
+               : "memory");
+}
+
+// Store 16 consecutive TMEM columns of this thread's lane (32x32b shape, x16).
+HOA_DEVICE void tmem_st16(uint32_t taddr, const float (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15]))
+      : "memory");
+}
+
+HOA_DEVICE void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Round to tf32 (nearest, ties away), returned in an fp32 container.
+HOA_DEVICE float to_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
 
 }  // namespace sm100
 }  // namespace hoa

@@ -114,3 +114,33 @@ def test_stages_equal_core_forward(dtype):
     y2 = ops.core_stages(a, qkv, H, 0.5, 1 / math.sqrt(d), dtype, dtype, chunk)
     torch.cuda.synchronize()
     assert torch.equal(y1, y2)
+
+
+@pytest.mark.parametrize("d", [8, 32, 48, 64, 96, 120])
+@pytest.mark.parametrize("scale", [0.01, 0.4])
+def test_link_local_vs_oracle(d, scale):
+    """Kernels (1)+(2): P_t = R_t C_k, the transports and the total against float64.
+
+    scale 0.4 per generator entry makes ||A|| large, so the exponential takes
+    the scaling-and-squaring branch (both the SIMT and the tensor-core kernel)."""
+    from oracle import holonomy_oracle as O
+    torch.manual_seed(d)
+    B, H, T, chunk = 1, 2, 19, 8
+    m = d * (d - 1) // 2
+    a = (scale * torch.randn(B, T, H * m)).float()
+    qkv = torch.randn(B, T, 3 * H * d).float()
+    R, U, M = ops.link_local(a.to(DEV), qkv.to(DEV), H, 1.0, chunk)
+    C, total = ops.carry_scan(M, want_total=True)
+    kidx = torch.arange(T, device=DEV) // chunk
+    P = torch.einsum("ntij,ntjk->ntik", R.double(), C[:, kidx].double()).cpu().numpy()
+    a64 = a.double().numpy().reshape(B, T, H, m).transpose(0, 2, 1, 3)          # (B,H,T,m)
+    G = O.expm(O.skew_from_vec(a64, d))                                          # (B,H,T,d,d)
+    Pref = O.prefix_products(G[:, :, :-1]).reshape(B * H, T, d, d)
+    tol = 1e-5 if scale < 0.1 else 1e-4
+    assert O.rel_l2(P, Pref) < tol
+    tot_ref = (G[:, :, -1] @ O.prefix_products(G[:, :, :-1])[:, :, -1]).reshape(B * H, d, d)
+    assert O.rel_l2(total.cpu().numpy(), tot_ref) < tol
+    q = qkv.double().numpy().reshape(B, T, H, 3 * d).transpose(0, 2, 1, 3).reshape(B * H, T, 3 * d)[..., :d]
+    qhat = torch.einsum("ntfe,ntf->nte", C[:, kidx].double(), U[:, :, 0].double()).cpu().numpy()
+    qref = np.einsum("ntde,ntd->nte", Pref, q)
+    assert O.rel_l2(qhat, qref) < tol
