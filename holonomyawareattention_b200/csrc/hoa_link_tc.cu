@@ -6,8 +6,9 @@
 // (core/utils.py:4-52, core/attention_fast_chunked.py:77, 86-94, 108-110);
 // this variant serves d in {32, 48, 64, 96} with fp32 generators.
 //
-// One CTA of 4 warps per (chain, chunk); thread r owns row r of every d x d
-// matrix (TMEM lane r = row r of every accumulator).  Every product D = X Y
+// One CTA per (chain, chunk): 4 TMEM lane groups x 4 (or 2) column groups of
+// warps; the thread at (lane group g, lane l, column group q) owns row 32g + l
+// (TMEM lane = row of every accumulator) and a quarter (or half) of its columns.  Every product D = X Y
 // takes X as rows (K-major) and Y as the rows of Y^T (K-major B operand), in
 // the 128B-swizzled layout; the matrices are polynomials in the skew A, so
 // p(A)^T = p(-A) gives most transposes for free:
@@ -21,15 +22,13 @@
 //       R_{t+1}^T = R^T + D1         (fp32, CUDA cores; R^T kept exactly in TMEM)
 // Keeping the identity out of every tensor-core product makes the MMA's own
 // accumulation rounding scale with the small delta (|N| ~ |A|), not with |G R|.
-// The running product lives in TMEM as R^T (fp32, and tf32 hi/lo columns), the
-// A operand the next composition needs.  A double-buffered generator vector is
+// The running product lives in TMEM as R^T split exactly into tf32 hi and the
+// fp32 remainder lo (R^T = hi + lo), the A operand the next composition needs.  A double-buffered generator vector is
 // fetched by 1-D bulk TMA copies.
 #include "hoa_sm100.cuh"
 
 namespace hoa {
 using namespace sm100;
-
-constexpr int kLtThreads = 128;
 
 // T8 coefficients (derivation in hoa_link.cu).
 __constant__ float kT8tc[8] = {
@@ -40,17 +39,25 @@ constexpr float kTheta8tc = 0.6f;
 
 template <int DP>
 struct LtLayout {
+  // Thread layout: 4 TMEM lane groups (warps w % 4) x CQ column groups (warps w / 4).
+  static constexpr int CQ = (DP % 32 == 0) ? 4 : 2;
+  static constexpr int CW = DP / CQ;                   // columns per thread
+  static constexpr int NCH = CW / 8;                   // 8-column chunks per thread
+  static constexpr int NT = 128 * CQ;
+  static_assert(CW % 8 == 0, "column groups must be multiples of 8");
   static constexpr int NSLAB = (DP + 31) / 32;
   static constexpr int kSlab = DP * 128;               // DP rows of 128 bytes
   static constexpr int kMat = NSLAB * kSlab;           // one split (hi or lo) of one matrix
   // An A operand is read as 128 rows (M = 128), i.e. 128 - DP rows past the
-  // end of its last slab; the transpose scratch that follows covers that.
+  // end of its last slab; the scratch that follows covers that.
   static constexpr int offYhi = 0;
   static constexpr int offYlo = kMat;
   static constexpr int offXhi = 2 * kMat;
   static constexpr int offXlo = 3 * kMat;
-  static constexpr int offXT = 4 * kMat;                 // fp32 [DP][DP+1] transpose scratch
-  static constexpr int kXTbytes = DP * (DP + 1) * 4;
+  static constexpr int offXT = 4 * kMat;               // fp32 scratch: [DP][DP+1] transpose, or reductions
+  static constexpr int kXTmat = DP * (DP + 1) * 4;
+  static constexpr int kXTred = CQ * 3 * 128 * 4;
+  static constexpr int kXTbytes = kXTmat > kXTred ? kXTmat : kXTred;
   static constexpr int kXend = offXlo + (NSLAB - 1) * kSlab + 128 * 128;
   static constexpr int kEnd0 = offXT + kXTbytes > kXend ? offXT + kXTbytes : kXend;
   static constexpr int offStage = (kEnd0 + 1023) / 1024 * 1024;
@@ -59,7 +66,7 @@ struct LtLayout {
   static constexpr int offRed = offVec + 3 * DP * 4;
   static constexpr int offBar = offRed + 64;
   static constexpr int kBytes = offBar + 64;
-  // TMEM: R^T hi, R^T lo, R^T fp32, D1, D2 (DP columns each), rounded up to a power of two.
+  // TMEM: R^T hi, R^T lo, A, D1, D2 (DP columns each), rounded up to a power of two.
   static constexpr uint32_t kTmemCols = 5 * DP <= 128 ? 128 : (5 * DP <= 256 ? 256 : 512);
   // Request enough shared memory that no more CTAs share an SM than its 512
   // TMEM columns can serve (an allocation would otherwise wait for a peer).
@@ -78,13 +85,13 @@ struct LinkTcArgs {
   int B, H, T, chunk, K;
 };
 
-// Row r, columns [c0, c0+16) of A = skew(edge_scale * a) from the staged vector.
+// Row r, columns [c0, c0+8) of A = skew(edge_scale * a) from the staged vector.
 // S_i = i (2d - i - 1) / 2 is the offset of row i's strict upper triangle.
 template <int DP>
-HOA_DEVICE void skew_row16(const float* __restrict__ av, float es, int r, int c0, float (&v)[16]) {
+HOA_DEVICE void skew_row8(const float* __restrict__ av, float es, int r, int c0, float (&v)[8]) {
   const int Sr = r * (2 * DP - r - 1) / 2;
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
+  for (int i = 0; i < 8; ++i) {
     const int c = c0 + i;
     float x = 0.f;
     if (c > r) x = __fmul_rn(av[Sr + c - r - 1], es);
@@ -93,20 +100,21 @@ HOA_DEVICE void skew_row16(const float* __restrict__ av, float es, int r, int c0
   }
 }
 
-// Write 16 values of row `row`, columns [c0, c0+16), as tf32 hi and lo into
-// two swizzled operand buffers (slab = c0 / 32).
+// Write 8 values of row `row`, columns [c0, c0+8), as tf32 hi (rounded) and
+// lo = x - hi (exact; the tensor core reads its leading tf32 bits) into two
+// swizzled operand buffers.
 template <int DP>
-HOA_DEVICE void put_row16(uint8_t* hi_buf, uint8_t* lo_buf, int row, int c0, const float (&v)[16]) {
+HOA_DEVICE void put_row8(uint8_t* hi_buf, uint8_t* lo_buf, int row, int c0, const float (&v)[8]) {
   using L = LtLayout<DP>;
   const int slab = c0 >> 5;
   const int ch0 = (c0 & 31) >> 2;
 #pragma unroll
-  for (int q = 0; q < 4; ++q) {
+  for (int q = 0; q < 2; ++q) {
     float h[4], l[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       h[i] = to_tf32(v[4 * q + i]);
-      l[i] = to_tf32(v[4 * q + i] - h[i]);
+      l[i] = v[4 * q + i] - h[i];
     }
     const uint32_t off = slab * L::kSlab + sw128_offset(row, ch0 + q);
     *reinterpret_cast<float4*>(hi_buf + off) = make_float4(h[0], h[1], h[2], h[3]);
@@ -135,7 +143,7 @@ HOA_DEVICE void issue_ss(uint32_t d_tmem, uint32_t xhi, uint32_t xlo, uint32_t y
 template <int DP>
 HOA_DEVICE void issue_ts(uint32_t d_tmem, uint32_t ahi, uint32_t alo, uint32_t bhi, uint32_t blo) {
   using L = LtLayout<DP>;
-  constexpr uint32_t id = make_idesc(kFmtTF32, 128, DP, false);
+  constexpr uint32_t id = make_idesc(kFmtTF32, 128, DP);
   const uint32_t as[3] = {ahi, ahi, alo};
   const uint32_t bs[3] = {bhi, blo, bhi};
 #pragma unroll
@@ -147,10 +155,19 @@ HOA_DEVICE void issue_ts(uint32_t d_tmem, uint32_t ahi, uint32_t alo, uint32_t b
     }
 }
 
+// Barrier for operand hand-over: generic shared-memory writes become visible
+// to the tensor core, TMEM accesses are ordered around the barrier.
+HOA_DEVICE void operand_barrier() {
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+}
+
 template <int DP>
-__global__ void __launch_bounds__(kLtThreads, 1) link_tc_kernel(LinkTcArgs p) {
+__global__ void __launch_bounds__(LtLayout<DP>::NT, 1) link_tc_kernel(LinkTcArgs p) {
   using L = LtLayout<DP>;
-  constexpr int NC = DP / 16;            // 16-column chunks of a row
+  constexpr int NCH = L::NCH, CW = L::CW, CQ = L::CQ, NT = L::NT;
   constexpr int m = DP * (DP - 1) / 2;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -167,8 +184,10 @@ __global__ void __launch_bounds__(kLtThreads, 1) link_tc_kernel(LinkTcArgs p) {
   uint64_t* bar_a = bar_mma + 1;                        // two: one per generator stage
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_a + 2);
 
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int r = tid;                                     // this thread's row
+  const int tid = threadIdx.x, warp = tid >> 5, lid = tid & 31;
+  const int g = warp & 3, q = warp >> 2;
+  const int r = g * 32 + lid;                            // this thread's row
+  const int c0 = q * CW;                                 // ... and its first column
   const bool row_ok = r < DP;
   const int chain = blockIdx.x / p.K;
   const int kc = blockIdx.x % p.K;
@@ -191,9 +210,9 @@ __global__ void __launch_bounds__(kLtThreads, 1) link_tc_kernel(LinkTcArgs p) {
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
-  const uint32_t lane = static_cast<uint32_t>(warp * 32) << 16;
-  const uint32_t cRhi = tbase, cRlo = tbase + DP, cD1 = tbase + 2 * DP, cD2 = tbase + 3 * DP,
-                 cRf = tbase + 4 * DP;
+  const uint32_t lane = static_cast<uint32_t>(g * 32) << 16;
+  const uint32_t cRhi = tbase, cRlo = tbase + DP, cA = tbase + 2 * DP, cD1 = tbase + 3 * DP,
+                 cD2 = tbase + 4 * DP;
   const uint32_t sXhi = smem_u32(Xhi), sXlo = smem_u32(Xlo), sYhi = smem_u32(Yhi),
                  sYlo = smem_u32(Ylo);
 
@@ -202,7 +221,7 @@ __global__ void __launch_bounds__(kLtThreads, 1) link_tc_kernel(LinkTcArgs p) {
   };
   auto load_vec = [&](int t) {     // q, k, v of position t into svec
     const long long qb = (((long long)b * p.T + t) * p.H + h) * 3LL * DP;
-    for (int i = tid; i < 3 * DP; i += kLtThreads) svec[i] = load_elem(p.qkv, qb + i, p.qkv_dtype);
+    for (int i = tid; i < 3 * DP; i += NT) svec[i] = load_elem(p.qkv, qb + i, p.qkv_dtype);
   };
 
   if (tid == 0) {
@@ -215,17 +234,16 @@ __global__ void __launch_bounds__(kLtThreads, 1) link_tc_kernel(LinkTcArgs p) {
   {
     const long long pos = (long long)chain * p.T + t0;
     float* Rg = p.R + pos * DP * DP;
-    for (int i = tid; i < DP * DP; i += kLtThreads) Rg[i] = (i / DP == i % DP) ? 1.f : 0.f;
+    for (int i = tid; i < DP * DP; i += NT) Rg[i] = (i / DP == i % DP) ? 1.f : 0.f;
     float* Ug = p.U + pos * 3 * DP;
-    for (int i = tid; i < 3 * DP; i += kLtThreads) Ug[i] = svec[i];
+    for (int i = tid; i < 3 * DP; i += NT) Ug[i] = svec[i];
 #pragma unroll
-    for (int c = 0; c < NC; ++c) {
-      float v[16], z[16];
+    for (int j = 0; j < NCH; ++j) {
+      float v[8], z[8];
 #pragma unroll
-      for (int i = 0; i < 16; ++i) { v[i] = (c * 16 + i == r) ? 1.f : 0.f; z[i] = 0.f; }
-      tmem_st16(cRhi + lane + c * 16, v);
-      tmem_st16(cRlo + lane + c * 16, z);
-      tmem_st16(cRf + lane + c * 16, v);
+      for (int i = 0; i < 8; ++i) { v[i] = (c0 + 8 * j + i == r) ? 1.f : 0.f; z[i] = 0.f; }
+      tmem_st8(cRhi + lane + c0 + 8 * j, v);
+      tmem_st8(cRlo + lane + c0 + 8 * j, z);
     }
     tmem_wait_st();
   }
@@ -237,7 +255,7 @@ __global__ void __launch_bounds__(kLtThreads, 1) link_tc_kernel(LinkTcArgs p) {
 
   for (int t = t0; t < t1; ++t) {
     const int sidx = (t - t0) & 1;
-    float* av = stage0 + sidx * (L::kStage / 4);
+    const float* av = stage0 + sidx * (L::kStage / 4);
     if (__syncthreads_or(bad)) { bad = true; break; }
     // prefetch the next edge's generator into the other stage (its readers are done)
     if (tid == 0 && t + 1 < t1) {
@@ -250,19 +268,20 @@ __global__ void __launch_bounds__(kLtThreads, 1) link_tc_kernel(LinkTcArgs p) {
     if (sidx == 0) { bad |= !mbar_wait(&bar_a[0], ph_a0); ph_a0 ^= 1; }
     else { bad |= !mbar_wait(&bar_a[1], ph_a1); ph_a1 ^= 1; }
 
-    // ---- P1: A rows -> X; D1 = A A^T = -A^2 ---------------------------------
-    if (row_ok) {
+    // ---- P1: A -> TMEM (fp32) and X rows; D1 = A A^T = -A^2 ---------------------
 #pragma unroll
-      for (int c = 0; c < NC; ++c) {
-        float v[16];
-        skew_row16<DP>(av, es, r, c * 16, v);
-        put_row16<DP>(Xhi, Xlo, r, c * 16, v);
+    for (int j = 0; j < NCH; ++j) {
+      float v[8];
+      if (row_ok) skew_row8<DP>(av, es, r, c0 + 8 * j, v);
+      else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = 0.f;
       }
+      tmem_st8(cA + lane + c0 + 8 * j, v);
+      if (row_ok) put_row8<DP>(Xhi, Xlo, r, c0 + 8 * j, v);
     }
-    fence_proxy_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
+    tmem_wait_st();
+    operand_barrier();
     if (tid == 0 && !bad) {
       issue_ss<DP>(cD1, sXhi, sXlo, sXhi, sXlo);
       tc_commit(bar_mma);
@@ -272,20 +291,28 @@ __global__ void __launch_bounds__(kLtThreads, 1) link_tc_kernel(LinkTcArgs p) {
     tc_fence_after();
 
     // ---- theta^2 = ||A^2||_1 (A^2 symmetric: max row abs-sum) ---------------
-    float rs = 0.f;
+    {
+      float rs = 0.f;
 #pragma unroll
-    for (int c = 0; c < NC; ++c) {
-      float v[16];
-      tmem_ld16(cD1 + lane + c * 16, v);
-      tmem_wait_ld();
+      for (int j = 0; j < NCH; ++j) {
+        float v[8];
+        tmem_ld8(cD1 + lane + c0 + 8 * j, v);
+        tmem_wait_ld();
 #pragma unroll
-      for (int i = 0; i < 16; ++i) rs += fabsf(v[i]);
+        for (int i = 0; i < 8; ++i) rs += fabsf(v[i]);
+      }
+      XT[q * 128 + r] = row_ok ? rs : 0.f;
+      __syncthreads();
+      if (q == 0) {
+        float full = 0.f;
+#pragma unroll
+        for (int qq = 0; qq < CQ; ++qq) full += XT[qq * 128 + r];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) full = fmaxf(full, __shfl_xor_sync(0xffffffffu, full, o));
+        if (lid == 0) sred[g] = full;
+      }
+      __syncthreads();
     }
-    if (!row_ok) rs = 0.f;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) rs = fmaxf(rs, __shfl_xor_sync(0xffffffffu, rs, o));
-    if ((tid & 31) == 0) sred[warp] = rs;
-    __syncthreads();
     int nsq = 0;
     {
       float theta = sqrtf(fmaxf(fmaxf(sred[0], sred[1]), fmaxf(sred[2], sred[3])));
@@ -294,29 +321,25 @@ __global__ void __launch_bounds__(kLtThreads, 1) link_tc_kernel(LinkTcArgs p) {
     const float sa = ldexpf(1.f, -nsq);
     const float sa2 = -ldexpf(1.f, -2 * nsq);    // A2s = -D1 * 4^-s
 
-    // ---- P2: X = A2s rows, Y^T = T1^T rows -----------------------------------
-    // (TMEM loads are warp-collective: every lane executes them, rows or not.)
+    // ---- P2: X = A2s rows, Y^T = T1^T = -x1 As + x2 A2s rows; D2 = A4 ------------
 #pragma unroll
-    for (int c = 0; c < NC; ++c) {
-      float a2[16];
-      tmem_ld16(cD1 + lane + c * 16, a2);
+    for (int j = 0; j < NCH; ++j) {
+      float a2[8], a[8];
+      tmem_ld8(cD1 + lane + c0 + 8 * j, a2);
+      tmem_ld8(cA + lane + c0 + 8 * j, a);
       tmem_wait_ld();
       if (row_ok) {
-        float a[16], t1v[16];
-        skew_row16<DP>(av, es, r, c * 16, a);
+        float t1v[8];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
+        for (int i = 0; i < 8; ++i) {
           a2[i] *= sa2;
-          t1v[i] = x2 * a2[i] - x1 * (a[i] * sa);             // row of T1^T
+          t1v[i] = x2 * a2[i] - x1 * (a[i] * sa);
         }
-        put_row16<DP>(Xhi, Xlo, r, c * 16, a2);
-        put_row16<DP>(Yhi, Ylo, r, c * 16, t1v);
+        put_row8<DP>(Xhi, Xlo, r, c0 + 8 * j, a2);
+        put_row8<DP>(Yhi, Ylo, r, c0 + 8 * j, t1v);
       }
     }
-    fence_proxy_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
+    operand_barrier();
     if (tid == 0 && !bad) {
       issue_ss<DP>(cD2, sXhi, sXlo, sYhi, sYlo);
       tc_commit(bar_mma);
@@ -325,31 +348,32 @@ __global__ void __launch_bounds__(kLtThreads, 1) link_tc_kernel(LinkTcArgs p) {
     ph_mma ^= 1;
     tc_fence_after();
 
-    // ---- A4 -> transpose scratch, so that each thread can read its row of A4^T
+    // ---- A4 -> transpose scratch, so that each thread can read its part of A4^T
 #pragma unroll
-    for (int c = 0; c < NC; ++c) {
-      float a4[16];
-      tmem_ld16(cD2 + lane + c * 16, a4);
+    for (int j = 0; j < NCH; ++j) {
+      float a4[8];
+      tmem_ld8(cD2 + lane + c0 + 8 * j, a4);
       tmem_wait_ld();
       if (row_ok) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) XT[r * (DP + 1) + c * 16 + i] = a4[i];
+        for (int i = 0; i < 8; ++i) XT[r * (DP + 1) + c0 + 8 * j + i] = a4[i];
       }
     }
     __syncthreads();
 
     // ---- P3: X = L rows, Y^T = F^T rows; N0 = As + (y2 + x3 x4) A2s + x4 A4 -> D1
 #pragma unroll
-    for (int c = 0; c < NC; ++c) {
-      float a2[16], a4[16], a[16], lv[16], fv[16], n0[16];
-      tmem_ld16(cD1 + lane + c * 16, a2);
-      tmem_ld16(cD2 + lane + c * 16, a4);
+    for (int j = 0; j < NCH; ++j) {
+      float a2[8], a4[8], a[8], n0[8];
+      tmem_ld8(cD1 + lane + c0 + 8 * j, a2);
+      tmem_ld8(cD2 + lane + c0 + 8 * j, a4);
+      tmem_ld8(cA + lane + c0 + 8 * j, a);
       tmem_wait_ld();
       if (row_ok) {
-        skew_row16<DP>(av, es, r, c * 16, a);
+        float lv[8], fv[8];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int col = c * 16 + i;
+        for (int i = 0; i < 8; ++i) {
+          const int col = c0 + 8 * j + i;
           const float a2s = a2[i] * sa2;
           const float as = a[i] * sa;
           const float a4t = XT[col * (DP + 1) + r];               // A4^T[r][col] = A4[col][r]
@@ -357,19 +381,16 @@ __global__ void __launch_bounds__(kLtThreads, 1) link_tc_kernel(LinkTcArgs p) {
           fv[i] = x6 * a2s + x7 * a4t - x5 * as;
           n0[i] = as + (y2 + x3 * x4) * a2s + x4 * a4[i];
         }
-        put_row16<DP>(Xhi, Xlo, r, c * 16, lv);
-        put_row16<DP>(Yhi, Ylo, r, c * 16, fv);
+        put_row8<DP>(Xhi, Xlo, r, c0 + 8 * j, lv);
+        put_row8<DP>(Yhi, Ylo, r, c0 + 8 * j, fv);
       } else {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) n0[i] = 0.f;
+        for (int i = 0; i < 8; ++i) n0[i] = 0.f;
       }
-      tmem_st16(cD1 + lane + c * 16, n0);
+      tmem_st8(cD1 + lane + c0 + 8 * j, n0);
     }
     tmem_wait_st();
-    fence_proxy_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
+    operand_barrier();
     if (tid == 0 && !bad) {
       issue_ss<DP>(cD2, sXhi, sXlo, sYhi, sYlo);        // D2 = L F
       tc_commit(bar_mma);
@@ -380,41 +401,38 @@ __global__ void __launch_bounds__(kLtThreads, 1) link_tc_kernel(LinkTcArgs p) {
 
     // ---- N = G - I = N0 + D2, then s squarings N <- 2N + N N; N rows -> Y -------
 #pragma unroll
-    for (int c = 0; c < NC; ++c) {
-      float n0[16], g[16];
-      tmem_ld16(cD1 + lane + c * 16, n0);
-      tmem_ld16(cD2 + lane + c * 16, g);
+    for (int j = 0; j < NCH; ++j) {
+      float n0[8], nv[8];
+      tmem_ld8(cD1 + lane + c0 + 8 * j, n0);
+      tmem_ld8(cD2 + lane + c0 + 8 * j, nv);
       tmem_wait_ld();
       if (row_ok) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) g[i] += n0[i];
+        for (int i = 0; i < 8; ++i) nv[i] += n0[i];
         if (nsq > 0) {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) XT[r * (DP + 1) + c * 16 + i] = g[i];
+          for (int i = 0; i < 8; ++i) XT[r * (DP + 1) + c0 + 8 * j + i] = nv[i];
         } else {
-          put_row16<DP>(Yhi, Ylo, r, c * 16, g);
+          put_row8<DP>(Yhi, Ylo, r, c0 + 8 * j, nv);
         }
       }
     }
     for (int sq = 0; sq < nsq; ++sq) {      // N <- 2N + N N: X = N rows, Y^T = N^T rows
-      __syncthreads();                       // N rows complete in the scratch
+      __syncthreads();                       // N complete in the scratch
       if (row_ok) {
 #pragma unroll
-        for (int c = 0; c < NC; ++c) {
-          float g[16], gt[16];
+        for (int j = 0; j < NCH; ++j) {
+          float nv[8], nt[8];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            g[i] = XT[r * (DP + 1) + c * 16 + i];
-            gt[i] = XT[(c * 16 + i) * (DP + 1) + r];
+          for (int i = 0; i < 8; ++i) {
+            nv[i] = XT[r * (DP + 1) + c0 + 8 * j + i];
+            nt[i] = XT[(c0 + 8 * j + i) * (DP + 1) + r];
           }
-          put_row16<DP>(Xhi, Xlo, r, c * 16, g);
-          put_row16<DP>(Yhi, Ylo, r, c * 16, gt);
+          put_row8<DP>(Xhi, Xlo, r, c0 + 8 * j, nv);
+          put_row8<DP>(Yhi, Ylo, r, c0 + 8 * j, nt);
         }
       }
-      fence_proxy_async_smem();
-      tc_fence_before();
-      __syncthreads();
-      tc_fence_after();
+      operand_barrier();
       if (tid == 0 && !bad) {
         issue_ss<DP>(cD2, sXhi, sXlo, sYhi, sYlo);
         tc_commit(bar_mma);
@@ -423,29 +441,23 @@ __global__ void __launch_bounds__(kLtThreads, 1) link_tc_kernel(LinkTcArgs p) {
       ph_mma ^= 1;
       tc_fence_after();
 #pragma unroll
-      for (int c = 0; c < NC; ++c) {
-        float g[16];
-        tmem_ld16(cD2 + lane + c * 16, g);
+      for (int j = 0; j < NCH; ++j) {
+        float nv[8];
+        tmem_ld8(cD2 + lane + c0 + 8 * j, nv);
         tmem_wait_ld();
         if (row_ok) {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) g[i] = fmaf(2.f, XT[r * (DP + 1) + c * 16 + i], g[i]);
-        }
-        __syncwarp();
-        if (row_ok) {
+          for (int i = 0; i < 8; ++i) nv[i] = fmaf(2.f, XT[r * (DP + 1) + c0 + 8 * j + i], nv[i]);
           if (sq + 1 < nsq) {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) XT[r * (DP + 1) + c * 16 + i] = g[i];
+            for (int i = 0; i < 8; ++i) XT[r * (DP + 1) + c0 + 8 * j + i] = nv[i];
           } else {
-            put_row16<DP>(Yhi, Ylo, r, c * 16, g);
+            put_row8<DP>(Yhi, Ylo, r, c0 + 8 * j, nv);
           }
         }
       }
     }
-    fence_proxy_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
+    operand_barrier();
 
     // ---- P4: D1 = R^T N^T ------------------------------------------------------
     if (tid == 0 && !bad) {
@@ -456,47 +468,59 @@ __global__ void __launch_bounds__(kLtThreads, 1) link_tc_kernel(LinkTcArgs p) {
     ph_mma ^= 1;
     tc_fence_after();
 
-    // ---- R_{t+1}^T = R^T + D1: keep it in TMEM (fp32, hi, lo); write R_{t+1}
-    //      and U_{t+1}, or the chunk total after the chunk's last edge.
+    // ---- R_{t+1}^T = R^T + D1 (R^T = hi + lo exactly); write R_{t+1}, U_{t+1},
+    //      or the chunk total after the chunk's last edge.
     const bool last = (t + 1 == t1);
     const long long pos1 = (long long)chain * p.T + t + 1;
     float* Rg = last ? p.M + ((long long)chain * p.K + kc) * DP * DP : p.R + pos1 * DP * DP;
     float u0 = 0.f, u1 = 0.f, u2 = 0.f;
 #pragma unroll
-    for (int c = 0; c < NC; ++c) {
-      float v[16], dv[16], hv[16], lv[16];
-      tmem_ld16(cRf + lane + c * 16, v);
-      tmem_ld16(cD1 + lane + c * 16, dv);
+    for (int j = 0; j < NCH; ++j) {
+      float rh[8], rl[8], dv[8];
+      tmem_ld8(cRhi + lane + c0 + 8 * j, rh);
+      tmem_ld8(cRlo + lane + c0 + 8 * j, rl);
+      tmem_ld8(cD1 + lane + c0 + 8 * j, dv);
       tmem_wait_ld();
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        v[i] += dv[i];
-        hv[i] = to_tf32(v[i]);
-        lv[i] = to_tf32(v[i] - hv[i]);
+      for (int i = 0; i < 8; ++i) {
+        const float v = (rh[i] + rl[i]) + dv[i];
+        rh[i] = to_tf32(v);
+        rl[i] = v - rh[i];
+        dv[i] = v;
       }
-      tmem_st16(cRf + lane + c * 16, v);
-      tmem_st16(cRhi + lane + c * 16, hv);
-      tmem_st16(cRlo + lane + c * 16, lv);
+      tmem_st8(cRhi + lane + c0 + 8 * j, rh);
+      tmem_st8(cRlo + lane + c0 + 8 * j, rl);
       if (row_ok) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int k = c * 16 + i;                 // v[i] = R_{t+1}[k][r]
-          Rg[(long long)k * DP + r] = v[i];
-          if (!last) {
-            u0 = fmaf(v[i], svec[k], u0);
-            u1 = fmaf(v[i], svec[DP + k], u1);
-            u2 = fmaf(v[i], svec[2 * DP + k], u2);
-          }
+        for (int i = 0; i < 8; ++i) {
+          const int k = c0 + 8 * j + i;                 // dv[i] = R_{t+1}[k][r]
+          Rg[(long long)k * DP + r] = dv[i];
+          u0 = fmaf(dv[i], svec[k], u0);
+          u1 = fmaf(dv[i], svec[DP + k], u1);
+          u2 = fmaf(dv[i], svec[2 * DP + k], u2);
         }
       }
     }
-    if (row_ok && !last) {
-      float* Ug = p.U + pos1 * 3 * DP;
-      Ug[r] = u0;
-      Ug[DP + r] = u1;
-      Ug[2 * DP + r] = u2;
-    }
     tmem_wait_st();
+    if (!last) {                                         // U_{t+1}: sum the column groups
+      XT[(q * 3 + 0) * 128 + r] = u0;
+      XT[(q * 3 + 1) * 128 + r] = u1;
+      XT[(q * 3 + 2) * 128 + r] = u2;
+      __syncthreads();
+      if (q == 0 && row_ok) {
+        float s0 = 0.f, s1 = 0.f, s2 = 0.f;
+#pragma unroll
+        for (int qq = 0; qq < CQ; ++qq) {
+          s0 += XT[(qq * 3 + 0) * 128 + r];
+          s1 += XT[(qq * 3 + 1) * 128 + r];
+          s2 += XT[(qq * 3 + 2) * 128 + r];
+        }
+        float* Ug = p.U + pos1 * 3 * DP;
+        Ug[r] = s0;
+        Ug[DP + r] = s1;
+        Ug[2 * DP + r] = s2;
+      }
+    }
     tc_fence_before();
   }
 
@@ -513,7 +537,7 @@ int launch_link_tc(const LinkTcArgs& a, cudaStream_t s) {
                            L::kAlloc) != cudaSuccess)
     return HOA_ERR_LAUNCH;
   const long long units = (long long)a.B * a.H * a.K;
-  link_tc_kernel<DP><<<(unsigned)units, kLtThreads, L::kAlloc, s>>>(a);
+  link_tc_kernel<DP><<<(unsigned)units, L::NT, L::kAlloc, s>>>(a);
   return launch_status();
 }
 
