@@ -131,18 +131,30 @@ class PathOrderedGeometricMHA(nn.Module):
         if x.dtype != torch.bfloat16:
             raise NotImplementedError(f"dtype {x.dtype} is not supported (float32 or bfloat16)")
         p2 = pair.reshape(B * L, 2 * D)
-        h = torch.mm(p2, lin0.weight.t(), out_dtype=torch.float32)
-        h = F.gelu(h.add_(lin0.bias.float()))
-        w2t = lin2.weight.t()
+        h = torch.addmm(lin0.bias.float(), p2, lin0.weight.t(), out_dtype=torch.float32)
+        h = F.gelu(h)
         hi = h.to(torch.bfloat16)
-        a = torch.mm(hi, w2t, out_dtype=torch.float32)
+        b2 = lin2.bias.float()
         if self.generator_precision == "split":
+            # [h_hi | h_lo] @ [W2^T ; W2^T]: one bf16 GEMM with K doubled, fp32 output,
+            # bias in the epilogue — the same sum as W2 h_hi + W2 h_lo + b2.
             lo = h.sub_(hi.float()).to(torch.bfloat16)
-            a.add_(torch.mm(lo, w2t, out_dtype=torch.float32))
-        elif self.generator_precision != "bf16":
+            a = torch.addmm(b2, torch.cat([hi, lo], dim=1), self._stacked_w2t(), out_dtype=torch.float32)
+        elif self.generator_precision == "bf16":
+            a = torch.addmm(b2, hi, lin2.weight.t(), out_dtype=torch.float32)
+        else:
             raise ValueError("generator_precision must be 'split' or 'bf16'")
-        a.add_(lin2.bias.float())
         return a.view(B, L, self.h * self.m_dim)
+
+    def _stacked_w2t(self) -> torch.Tensor:
+        """[W2^T ; W2^T] (8D, m*H), cached until edge_mlp.2.weight changes."""
+        w = self.edge_mlp[2].weight
+        key = (w.data_ptr(), w._version, w.dtype, str(w.device))
+        if getattr(self, "_w2cat_key", None) != key:
+            wt = w.t()
+            self._w2cat = torch.cat([wt, wt], dim=0).contiguous()
+            self._w2cat_key = key
+        return self._w2cat
 
     def forward(self, x: torch.Tensor, attn_mask: Optional[torch.Tensor] = None,
                 return_geometry: bool = False):

@@ -159,3 +159,20 @@ def test_deterministic_and_rejects():
         bad[5, 0] = False
         with pytest.raises(NotImplementedError):
             m(x, attn_mask=bad)
+
+
+@pytest.mark.parametrize("precision,tol", [("split", 3e-5), ("bf16", 6e-3)])
+def test_edge_generators_bf16_precision(precision, tol):
+    """bf16 module: generators (edge MLP output) against the fp32 MLP on the same bf16 values."""
+    B, T, D, H = 2, 64, 192, 4
+    sd, x = seeded_case(D, H, seed=7, B=B, L=T, bf16_round=True)
+    m = PathOrderedGeometricMHA(D, n_heads=H, edge_scale=0.05)
+    m.load_state_dict(sd)
+    m = m.to(DEV, torch.bfloat16).eval()
+    m.generator_precision = precision
+    with torch.no_grad():
+        a = m.edge_generators(x.to(DEV, torch.bfloat16)).float().cpu().numpy()
+    p = params_of(sd, np.float64)
+    ref = O.edge_generators(p, x.numpy().astype(np.float64), H, 1.0)        # (B,H,T,m)
+    ref = ref.transpose(0, 2, 1, 3).reshape(B, T, -1)
+    assert O.rel_l2(a, ref) < tol
