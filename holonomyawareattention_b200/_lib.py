@@ -23,10 +23,10 @@ SIGNATURES = {
     "hoa_status_string": (ctypes.c_char_p, [c_int]),
     "hoa_plan_chunk": (c_int, [c_int, c_int, c_int, c_int, c_int]),
     "hoa_core_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int, c_int]),
-    "hoa_core_forward": (c_int, [c_void_p, c_int, c_float, c_void_p, c_int, c_void_p, c_int, c_int,
+    "hoa_core_forward": (c_int, [c_void_p, c_int, c_void_p, c_float, c_void_p, c_int, c_void_p, c_int, c_int,
                                  c_float, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
                                  c_void_p, c_size_t, c_void_p]),
-    "hoa_link_local": (c_int, [c_void_p, c_int, c_float, c_void_p, c_int, c_void_p, c_void_p,
+    "hoa_link_local": (c_int, [c_void_p, c_int, c_void_p, c_float, c_void_p, c_int, c_void_p, c_void_p,
                                c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p]),
     "hoa_carry_scan": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
                                c_void_p]),
@@ -39,7 +39,7 @@ SIGNATURES = {
                                 c_int, c_int, c_void_p]),
     "hoa_out_transport": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_int,
                                   c_int, c_int, c_int, c_void_p]),
-    "hoa_core_forward_noalloc": (c_int, [c_void_p, c_int, c_float, c_void_p, c_int, c_void_p, c_int,
+    "hoa_core_forward_noalloc": (c_int, [c_void_p, c_int, c_void_p, c_float, c_void_p, c_int, c_void_p, c_int,
                                          c_int, c_float, c_void_p, c_void_p, c_int, c_int, c_int,
                                          c_int, c_int, c_void_p]),
 }

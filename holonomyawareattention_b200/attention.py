@@ -45,9 +45,10 @@ class PathOrderedGeometricMHA(nn.Module):
     ``generator_precision`` (not in the reference) controls how the edge
     generators are produced when the module runs in bfloat16:
       * "split" (default): the edge-MLP hidden layer is kept in fp32 and the
-        second GEMM runs as two bf16 GEMMs (high and low halves of the hidden
-        activations) with fp32 output, so the generators carry ~16 bits and
-        long rotation products do not drift;
+        second GEMM runs as one bf16 GEMM over the high and low bf16 halves of
+        the hidden activations ([h_hi | h_lo] against [W2^T ; W2^T]) with fp32
+        output, so the generators carry ~16 bits and long rotation products
+        do not drift;
       * "bf16": one bf16 GEMM with fp32 output (hidden activations rounded to
         bf16); about 1e-3 relative error per generator entry, which grows as
         sqrt(T) along the path product.
@@ -123,28 +124,34 @@ class PathOrderedGeometricMHA(nn.Module):
         core/attention_fast_chunked.py:73-76 (the edge_scale multiply happens in
         the link kernel).
         """
+        a, bias = self._edge_generators_nobias(x)
+        return a if bias is None else a + bias
+
+    def _edge_generators_nobias(self, x: torch.Tensor):
+        """(a_all without the MLP's output bias, that bias or None): the link
+        kernel adds the bias while it stages each generator, so the large fp32
+        output is written once by the GEMM and never touched again."""
         B, L, D = x.shape
         pair = torch.cat([x, torch.roll(x, shifts=-1, dims=1)], dim=-1)
         lin0, lin2 = self.edge_mlp[0], self.edge_mlp[2]
         if x.dtype == torch.float32:
-            return self.edge_mlp(pair)
+            return self.edge_mlp(pair), None
         if x.dtype != torch.bfloat16:
             raise NotImplementedError(f"dtype {x.dtype} is not supported (float32 or bfloat16)")
         p2 = pair.reshape(B * L, 2 * D)
         h = torch.addmm(lin0.bias.float(), p2, lin0.weight.t(), out_dtype=torch.float32)
         h = F.gelu(h)
         hi = h.to(torch.bfloat16)
-        b2 = lin2.bias.float()
         if self.generator_precision == "split":
-            # [h_hi | h_lo] @ [W2^T ; W2^T]: one bf16 GEMM with K doubled, fp32 output,
-            # bias in the epilogue — the same sum as W2 h_hi + W2 h_lo + b2.
+            # [h_hi | h_lo] @ [W2^T ; W2^T]: one bf16 GEMM with K doubled and fp32
+            # output — the same sum as W2 h_hi + W2 h_lo.
             lo = h.sub_(hi.float()).to(torch.bfloat16)
-            a = torch.addmm(b2, torch.cat([hi, lo], dim=1), self._stacked_w2t(), out_dtype=torch.float32)
+            a = torch.mm(torch.cat([hi, lo], dim=1), self._stacked_w2t(), out_dtype=torch.float32)
         elif self.generator_precision == "bf16":
-            a = torch.addmm(b2, hi, lin2.weight.t(), out_dtype=torch.float32)
+            a = torch.mm(hi, lin2.weight.t(), out_dtype=torch.float32)
         else:
             raise ValueError("generator_precision must be 'split' or 'bf16'")
-        return a.view(B, L, self.h * self.m_dim)
+        return a.view(B, L, self.h * self.m_dim), lin2.bias.float().contiguous()
 
     def _stacked_w2t(self) -> torch.Tensor:
         """[W2^T ; W2^T] (8D, m*H), cached until edge_mlp.2.weight changes."""
@@ -163,8 +170,9 @@ class PathOrderedGeometricMHA(nn.Module):
         qkv = self.qkv(x)
         if not qkv.is_contiguous():
             qkv = qkv.contiguous()
-        a_all = self.edge_generators(x)
+        a_all, a_bias = self._edge_generators_nobias(x)
         heads = ops.core_forward(a_all, qkv, self.h, self.edge_scale, self.scale,
-                                 out_dtype=x.dtype, hat_dtype=x.dtype, chunk=self.chunk)
+                                 out_dtype=x.dtype, hat_dtype=x.dtype, chunk=self.chunk,
+                                 a_bias=a_bias)
         y = self.out(heads)
         return y, None

@@ -124,7 +124,7 @@ HOA_DEVICE int triu_row(int idx, int d) {
 }
 
 struct LinkArgs {
-  const void* a; int a_dtype; float edge_scale;
+  const void* a; int a_dtype; const float* a_bias; float edge_scale;
   const void* qkv; int qkv_dtype;
   float* R; float* U; float* M;
   int B, H, T, d, chunk, K;
@@ -176,7 +176,9 @@ __global__ void __launch_bounds__(LinkCfg<DP>::NT, 1) link_local_kernel(LinkArgs
     for (int idx = tid; idx < m; idx += NT) {
       const int i = triu_row(idx, d);
       const int j = idx - i * (2 * d - i - 1) / 2 + i + 1;
-      const float v = __fmul_rn(load_elem(p.a, abase + idx, p.a_dtype), p.edge_scale);
+      float av = load_elem(p.a, abase + idx, p.a_dtype);
+      if (p.a_bias != nullptr) av += p.a_bias[(long long)h * m + idx];
+      const float v = __fmul_rn(av, p.edge_scale);
       bufA[i * DP + j] = v;
       bufA[j * DP + i] = -v;
     }
@@ -367,48 +369,109 @@ carry_scan_kernel(const float* __restrict__ M, const float* __restrict__ carry_i
 // hat_v[t] = C_k^T U_v[t] for v in {q, k, v}.  One CTA per (chain, chunk).
 // q^ and k^ are written (B*H, T, d); v^ likewise, or transposed as
 // (B*H, d, vt_stride) when vt_stride > 0 (the K-major layout the tensor-core
-// attention reads for its P V product).
-constexpr int kApplyThreads = 256;
-constexpr int kApplyPos = 32;   // positions staged per step
+// attention reads for its P V product).  Each step is a [96 x DP] x [DP x DP]
+// product: rows = 32 positions x (q, k, v), register-tiled 6 x TN per thread.
+constexpr int kApplyPos = 32;
+constexpr int kApplyRows = 3 * kApplyPos;                 // 96
+constexpr int kApplyLd = kApplyRows + 4;                  // row stride of the transposed U tile
 
-__global__ void __launch_bounds__(kApplyThreads)
+template <int DP> struct ApplyCfg {
+  static constexpr int TN = DP >= 120 ? 8 : (DP >= 96 ? 6 : (DP >= 64 ? 4 : (DP >= 48 ? 3 : (DP >= 32 ? 2 : 1))));
+  static constexpr int CG = DP / TN;                      // column groups
+  static constexpr int TR = 6;                            // rows per thread
+  static constexpr int RG = kApplyRows / TR;              // 16 row groups
+  static constexpr int ACTIVE = RG * CG;
+  static constexpr int NT = ((ACTIVE + 31) / 32) * 32;
+  static constexpr size_t kSmem = (size_t)(DP * DP + DP * kApplyLd + DP * kApplyPos) * sizeof(float);
+};
+
+template <int DP>
+__global__ void __launch_bounds__(ApplyCfg<DP>::NT)
 carry_apply_kernel(const float* __restrict__ U, const float* __restrict__ Cin, void* qh, void* kh,
                    void* vh, int hat_dtype, int vt_stride, int T, int d, int chunk, int K) {
+  using Cf = ApplyCfg<DP>;
+  constexpr int TN = Cf::TN, TR = Cf::TR, NT = Cf::NT;
   extern __shared__ __align__(16) float smem[];
-  float* Cs = smem;                      // d*d, row-major
-  float* Us = Cs + d * d;                // kApplyPos * 3 * d
-  float* Vt = Us + kApplyPos * 3 * d;    // d * kApplyPos (transposed v^)
+  float* Cs = smem;                      // [DP][DP]: C_k, zero-padded
+  float* Ut = Cs + DP * DP;              // [DP][kApplyLd]: U tile transposed (r, row = pos*3 + v)
+  float* Vt = Ut + DP * kApplyLd;        // [DP][kApplyPos]: v^ staged for the transposed write
   const int tid = threadIdx.x;
   const int chain = blockIdx.x / K;
   const int kc = blockIdx.x % K;
   const int t0 = kc * chunk, t1 = min(t0 + chunk, T);
+  const bool active = tid < Cf::ACTIVE;
+  const int rg = tid / Cf::CG, cg = tid % Cf::CG;
+  const int row0 = rg * TR, col0 = cg * TN;
   const float* Cg = Cin + ((long long)chain * K + kc) * d * d;
-  for (int i = tid; i < d * d; i += kApplyThreads) Cs[i] = Cg[i];
-  void* outs[3] = {qh, kh, vh};
-  const int nvec = vt_stride > 0 ? 2 : 3;
+  for (int i = tid; i < DP * DP; i += NT) {
+    const int r = i / DP, e = i % DP;
+    Cs[i] = (r < d && e < d) ? Cg[r * d + e] : 0.f;
+  }
   for (int tb = t0; tb < t1; tb += kApplyPos) {
     const int np = min(kApplyPos, t1 - tb);
     __syncthreads();
     const float* Ug = U + ((long long)chain * T + tb) * 3 * d;
-    for (int i = tid; i < np * 3 * d; i += kApplyThreads) Us[i] = Ug[i];
+    for (int i = tid; i < kApplyRows * DP; i += NT) {
+      const int row = i / DP, r = i % DP;           // row = pos*3 + v
+      const int pp = row / 3;
+      Ut[r * kApplyLd + row] = (pp < np && r < d) ? Ug[(long long)row * d + r] : 0.f;
+    }
     __syncthreads();
-    for (int i = tid; i < np * 3 * d; i += kApplyThreads) {
-      const int e = i % d, v = (i / d) % 3, pp = i / (3 * d);
-      const float* u = Us + (pp * 3 + v) * d;
-      float s = 0.f;
-      for (int r = 0; r < d; ++r) s = fmaf(Cs[r * d + e], u[r], s);
-      if (v < nvec) store_elem(outs[v], ((long long)chain * T + tb + pp) * d + e, hat_dtype, s);
-      else Vt[e * kApplyPos + pp] = s;
+    float acc[TR][TN];
+#pragma unroll
+    for (int i = 0; i < TR; ++i)
+#pragma unroll
+      for (int j = 0; j < TN; ++j) acc[i][j] = 0.f;
+    if (active) {
+#pragma unroll 4
+      for (int r = 0; r < DP; ++r) {
+        float xa[TR], yb[TN];
+#pragma unroll
+        for (int i = 0; i < TR; ++i) xa[i] = Ut[r * kApplyLd + row0 + i];
+#pragma unroll
+        for (int j = 0; j < TN; ++j) yb[j] = Cs[r * DP + col0 + j];
+#pragma unroll
+        for (int i = 0; i < TR; ++i)
+#pragma unroll
+          for (int j = 0; j < TN; ++j) acc[i][j] = fmaf(xa[i], yb[j], acc[i][j]);
+      }
+#pragma unroll
+      for (int i = 0; i < TR; ++i) {
+        const int row = row0 + i, pp = row / 3, v = row % 3;
+        if (pp >= np) continue;
+#pragma unroll
+        for (int j = 0; j < TN; ++j) {
+          const int e = col0 + j;
+          if (e >= d) continue;
+          if (v < 2) store_elem(v == 0 ? qh : kh, ((long long)chain * T + tb + pp) * d + e, hat_dtype, acc[i][j]);
+          else if (vt_stride > 0) Vt[e * kApplyPos + pp] = acc[i][j];
+          else store_elem(vh, ((long long)chain * T + tb + pp) * d + e, hat_dtype, acc[i][j]);
+        }
+      }
     }
     if (vt_stride > 0) {
       __syncthreads();
-      for (int i = tid; i < d * kApplyPos; i += kApplyThreads) {
+      for (int i = tid; i < d * kApplyPos; i += NT) {
         const int e = i / kApplyPos, pp = i % kApplyPos;
         if (pp < np)
-          store_elem(vh, ((long long)chain * d + e) * vt_stride + tb + pp, hat_dtype, Vt[i]);
+          store_elem(vh, ((long long)chain * d + e) * vt_stride + tb + pp, hat_dtype, Vt[e * kApplyPos + pp]);
       }
     }
   }
+}
+
+template <int DP>
+int launch_carry_apply(const float* U, const float* C, void* qh, void* kh, void* vh,
+                       int hat_dtype, int vt_stride, int BH, int T, int d, int chunk,
+                       cudaStream_t s) {
+  using Cf = ApplyCfg<DP>;
+  if (cudaFuncSetAttribute(carry_apply_kernel<DP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)Cf::kSmem) != cudaSuccess)
+    return HOA_ERR_LAUNCH;
+  const int K = ceil_div(T, chunk);
+  carry_apply_kernel<DP><<<(unsigned)((long long)BH * K), Cf::NT, Cf::kSmem, s>>>(
+      U, C, qh, kh, vh, hat_dtype, vt_stride, T, d, chunk, K);
+  return launch_status();
 }
 
 template <int DP>
@@ -474,24 +537,24 @@ extern "C" int hoa_plan_chunk(int B, int H, int T, int d, int num_sms) {
 }
 
 namespace hoa {
-int link_local_tc(const void* a_all, int a_dtype, float edge_scale, const void* qkv,
+int link_local_tc(const void* a_all, int a_dtype, const float* a_bias, float edge_scale, const void* qkv,
                   int qkv_dtype, float* R, float* U, float* M, int* status, int B, int H, int T,
                   int d, int chunk, cudaStream_t s);
 }
 
 // The tensor-core kernel serves d in {32, 48, 64, 96} with fp32 generators; every
 // other shape runs the SIMT kernel.  Both compute the same fp32-accurate result.
-static int link_local_dispatch(const void* a_all, int a_dtype, float edge_scale, const void* qkv,
+static int link_local_dispatch(const void* a_all, int a_dtype, const float* a_bias, float edge_scale, const void* qkv,
                                int qkv_dtype, float* R, float* U, float* M, int* status, int B,
                                int H, int T, int d, int chunk, void* stream) {
   if (!a_all || !qkv || !R || !U || !M || B < 1 || H < 1 || T < 1 || d < 1 || chunk < 1)
     return HOA_ERR_INVALID_ARG;
   if (!valid_dtype(a_dtype) || !valid_dtype(qkv_dtype)) return HOA_ERR_UNSUPPORTED;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const int tc = link_local_tc(a_all, a_dtype, edge_scale, qkv, qkv_dtype, R, U, M, status, B, H,
-                               T, d, chunk, s);
+  const int tc = link_local_tc(a_all, a_dtype, a_bias, edge_scale, qkv, qkv_dtype, R, U, M, status,
+                               B, H, T, d, chunk, s);
   if (tc != HOA_ERR_UNSUPPORTED) return tc;
-  LinkArgs a{a_all, a_dtype, edge_scale, qkv, qkv_dtype, R, U, M, B, H, T, d, chunk,
+  LinkArgs a{a_all, a_dtype, a_bias, edge_scale, qkv, qkv_dtype, R, U, M, B, H, T, d, chunk,
              ceil_div(T, chunk)};
   switch (padded_dim(d)) {
     case 8: return launch_link_local<8>(a, s);
@@ -505,11 +568,11 @@ static int link_local_dispatch(const void* a_all, int a_dtype, float edge_scale,
   }
 }
 
-extern "C" int hoa_link_local(const void* a_all, int a_dtype, float edge_scale, const void* qkv,
-                              int qkv_dtype, float* R, float* U, float* M, int B, int H, int T,
-                              int d, int chunk, void* stream) {
-  return link_local_dispatch(a_all, a_dtype, edge_scale, qkv, qkv_dtype, R, U, M, nullptr, B, H,
-                             T, d, chunk, stream);
+extern "C" int hoa_link_local(const void* a_all, int a_dtype, const float* a_bias,
+                              float edge_scale, const void* qkv, int qkv_dtype, float* R, float* U,
+                              float* M, int B, int H, int T, int d, int chunk, void* stream) {
+  return link_local_dispatch(a_all, a_dtype, a_bias, edge_scale, qkv, qkv_dtype, R, U, M, nullptr,
+                             B, H, T, d, chunk, stream);
 }
 
 extern "C" int hoa_carry_scan(const float* M, const float* carry_in, float* C, float* total_out,
@@ -534,17 +597,18 @@ extern "C" int hoa_carry_apply(const float* U, const float* C, void* qh, void* k
   if (!U || !C || !qh || !kh || !vh || BH < 1 || T < 1 || d < 1 || chunk < 1)
     return HOA_ERR_INVALID_ARG;
   if (!valid_dtype(hat_dtype)) return HOA_ERR_UNSUPPORTED;
-  if (padded_dim(d) == 0) return HOA_ERR_UNSUPPORTED;
   if (vt_stride != 0 && vt_stride < T) return HOA_ERR_INVALID_ARG;
-  const int K = ceil_div(T, chunk);
-  const size_t smem = (size_t)(d * d + kApplyPos * 3 * d + d * kApplyPos) * sizeof(float);
-  if (cudaFuncSetAttribute(carry_apply_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)smem) != cudaSuccess)
-    return HOA_ERR_LAUNCH;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  carry_apply_kernel<<<(unsigned)((long long)BH * K), kApplyThreads, smem, s>>>(
-      U, C, qh, kh, vh, hat_dtype, vt_stride, T, d, chunk, K);
-  return launch_status();
+  switch (padded_dim(d)) {
+    case 8: return launch_carry_apply<8>(U, C, qh, kh, vh, hat_dtype, vt_stride, BH, T, d, chunk, s);
+    case 16: return launch_carry_apply<16>(U, C, qh, kh, vh, hat_dtype, vt_stride, BH, T, d, chunk, s);
+    case 32: return launch_carry_apply<32>(U, C, qh, kh, vh, hat_dtype, vt_stride, BH, T, d, chunk, s);
+    case 48: return launch_carry_apply<48>(U, C, qh, kh, vh, hat_dtype, vt_stride, BH, T, d, chunk, s);
+    case 64: return launch_carry_apply<64>(U, C, qh, kh, vh, hat_dtype, vt_stride, BH, T, d, chunk, s);
+    case 96: return launch_carry_apply<96>(U, C, qh, kh, vh, hat_dtype, vt_stride, BH, T, d, chunk, s);
+    case 120: return launch_carry_apply<120>(U, C, qh, kh, vh, hat_dtype, vt_stride, BH, T, d, chunk, s);
+    default: return HOA_ERR_UNSUPPORTED;
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -590,7 +654,8 @@ extern "C" size_t hoa_core_workspace_bytes(int B, int H, int T, int d, int chunk
   return core_layout(B, H, T, d, chunk, hat_dtype).total;
 }
 
-extern "C" int hoa_core_forward(const void* a_all, int a_dtype, float edge_scale, const void* qkv,
+extern "C" int hoa_core_forward(const void* a_all, int a_dtype, const float* a_bias,
+                                float edge_scale, const void* qkv,
                                 int qkv_dtype, void* out, int out_dtype, int hat_dtype,
                                 float softmax_scale, const float* carry_in, float* total_out,
                                 int B, int H, int T, int d, int chunk, void* workspace,
@@ -616,8 +681,8 @@ extern "C" int hoa_core_forward(const void* a_all, int a_dtype, float edge_scale
   const int K = ceil_div(T, chunk);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (cudaMemsetAsync(status, 0, sizeof(int), s) != cudaSuccess) return HOA_ERR_LAUNCH;
-  int st = link_local_dispatch(a_all, a_dtype, edge_scale, qkv, qkv_dtype, R, U, M, status, B, H,
-                               T, d, chunk, stream);
+  int st = link_local_dispatch(a_all, a_dtype, a_bias, edge_scale, qkv, qkv_dtype, R, U, M,
+                               status, B, H, T, d, chunk, stream);
   if (st != HOA_OK) return st;
   st = hoa_carry_scan(M, carry_in, C, total_out, B * H, K, d, stream);
   if (st != HOA_OK) return st;

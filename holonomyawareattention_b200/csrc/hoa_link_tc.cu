@@ -23,8 +23,11 @@
 // Keeping the identity out of every tensor-core product makes the MMA's own
 // accumulation rounding scale with the small delta (|N| ~ |A|), not with |G R|.
 // The running product lives in TMEM as R^T split exactly into tf32 hi and the
-// fp32 remainder lo (R^T = hi + lo), the A operand the next composition needs.  A double-buffered generator vector is
-// fetched by 1-D bulk TMA copies.
+// fp32 remainder lo (R^T = hi + lo), the A operand the next composition needs.
+// The generator and q, k, v of the next position arrive by 1-D bulk TMA copies
+// into a double-buffered stage; the next position's A-build and its P1 run
+// while the current composition P4 and its readout complete (two commit
+// barriers, alternating TMEM roles).
 #include "hoa_sm100.cuh"
 
 namespace hoa {
@@ -61,9 +64,10 @@ struct LtLayout {
   static constexpr int kXend = offXlo + (NSLAB - 1) * kSlab + 128 * 128;
   static constexpr int kEnd0 = offXT + kXTbytes > kXend ? offXT + kXTbytes : kXend;
   static constexpr int offStage = (kEnd0 + 1023) / 1024 * 1024;
-  static constexpr int kStage = ((DP * (DP - 1) / 2) * 4 + 127) / 128 * 128;
-  static constexpr int offVec = offStage + 2 * kStage;
-  static constexpr int offRed = offVec + 3 * DP * 4;
+  // one stage: the generator a_t (fp32) followed by q, k, v of position t (up to fp32)
+  static constexpr int kGenBytes = (DP * (DP - 1) / 2) * 4;
+  static constexpr int kStage = (kGenBytes + 3 * DP * 4 + 127) / 128 * 128;
+  static constexpr int offRed = offStage + 2 * kStage;
   static constexpr int offBar = offRed + 64;
   static constexpr int kBytes = offBar + 64;
   // TMEM: R^T hi, R^T lo, A, D1, D2 (DP columns each), rounded up to a power of two.
@@ -78,7 +82,7 @@ struct LtLayout {
 };
 
 struct LinkTcArgs {
-  const float* a; float edge_scale;
+  const float* a; const float* a_bias; float edge_scale;
   const void* qkv; int qkv_dtype;
   float* R; float* U; float* M;
   int* status;
@@ -177,11 +181,11 @@ __global__ void __launch_bounds__(LtLayout<DP>::NT, 1) link_tc_kernel(LinkTcArgs
   uint8_t* Xhi = sm + L::offXhi;
   uint8_t* Xlo = sm + L::offXlo;
   float* XT = reinterpret_cast<float*>(sm + L::offXT);
-  float* stage0 = reinterpret_cast<float*>(sm + L::offStage);
-  float* svec = reinterpret_cast<float*>(sm + L::offVec);
+  uint8_t* stage_base = sm + L::offStage;
   float* sred = reinterpret_cast<float*>(sm + L::offRed);
-  uint64_t* bar_mma = reinterpret_cast<uint64_t*>(sm + L::offBar);
-  uint64_t* bar_a = bar_mma + 1;                        // two: one per generator stage
+  uint64_t* bar_mma = reinterpret_cast<uint64_t*>(sm + L::offBar);  // P2, P3, squarings, P4
+  uint64_t* bar_p1 = bar_mma + 1;                                    // P1
+  uint64_t* bar_a = bar_mma + 2;                                     // two: one per stage
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_a + 2);
 
   const int tid = threadIdx.x, warp = tid >> 5, lid = tid & 31;
@@ -195,9 +199,12 @@ __global__ void __launch_bounds__(LtLayout<DP>::NT, 1) link_tc_kernel(LinkTcArgs
   const int t0 = kc * p.chunk;
   const int t1 = min(t0 + p.chunk, p.T);
   const float es = p.edge_scale;
+  const int qkv_bytes = 3 * DP * (p.qkv_dtype == HOA_BF16 ? 2 : 4);
+  const uint32_t stage_tx = (uint32_t)(L::kGenBytes + qkv_bytes);
 
   if (tid == 0) {
     mbar_init(bar_mma, 1);
+    mbar_init(bar_p1, 1);
     mbar_init(&bar_a[0], 1);
     mbar_init(&bar_a[1], 1);
     fence_mbar_init();
@@ -216,59 +223,35 @@ __global__ void __launch_bounds__(LtLayout<DP>::NT, 1) link_tc_kernel(LinkTcArgs
   const uint32_t sXhi = smem_u32(Xhi), sXlo = smem_u32(Xlo), sYhi = smem_u32(Yhi),
                  sYlo = smem_u32(Ylo);
 
-  auto gen_ptr = [&](int t) {
-    return p.a + (((long long)b * p.T + t) * p.H + h) * (long long)m;
+  auto stage_gen = [&](int s) { return reinterpret_cast<float*>(stage_base + s * L::kStage); };
+  auto stage_qkv = [&](int s) { return stage_base + s * L::kStage + L::kGenBytes; };
+  auto fetch = [&](int s, int t) {        // thread 0: a_t and (q, k, v)_t into stage s
+    const long long row = ((long long)b * p.T + t) * p.H + h;
+    mbar_arrive_expect_tx(&bar_a[s], stage_tx);
+    bulk_load(stage_gen(s), p.a + row * m, L::kGenBytes, &bar_a[s]);
+    bulk_load(stage_qkv(s),
+              static_cast<const uint8_t*>(p.qkv) + row * (long long)qkv_bytes, qkv_bytes, &bar_a[s]);
   };
-  auto load_vec = [&](int t) {     // q, k, v of position t into svec
-    const long long qb = (((long long)b * p.T + t) * p.H + h) * 3LL * DP;
-    for (int i = tid; i < 3 * DP; i += NT) svec[i] = load_elem(p.qkv, qb + i, p.qkv_dtype);
+  // the generator bias of this chain's head, held in registers (a few per thread)
+  constexpr int kBiasPer = (m + NT - 1) / NT;
+  float breg[kBiasPer];
+#pragma unroll
+  for (int k = 0; k < kBiasPer; ++k) {
+    const int i = tid + k * NT;
+    breg[k] = (p.a_bias != nullptr && i < m) ? p.a_bias[(long long)h * m + i] : 0.f;
+  }
+  auto add_bias = [&](int s) {            // all threads; a barrier must follow
+    if (p.a_bias == nullptr) return;
+    float* av = stage_gen(s);
+#pragma unroll
+    for (int k = 0; k < kBiasPer; ++k) {
+      const int i = tid + k * NT;
+      if (i < m) av[i] += breg[k];
+    }
   };
-
-  if (tid == 0) {
-    mbar_arrive_expect_tx(&bar_a[0], m * 4);
-    bulk_load(stage0, gen_ptr(t0), m * 4, &bar_a[0]);
-  }
-  // position t0: R = I, U = (q, k, v); R^T = I in TMEM (hi = I, lo = 0)
-  load_vec(t0);
-  __syncthreads();
-  {
-    const long long pos = (long long)chain * p.T + t0;
-    float* Rg = p.R + pos * DP * DP;
-    for (int i = tid; i < DP * DP; i += NT) Rg[i] = (i / DP == i % DP) ? 1.f : 0.f;
-    float* Ug = p.U + pos * 3 * DP;
-    for (int i = tid; i < 3 * DP; i += NT) Ug[i] = svec[i];
-#pragma unroll
-    for (int j = 0; j < NCH; ++j) {
-      float v[8], z[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) { v[i] = (c0 + 8 * j + i == r) ? 1.f : 0.f; z[i] = 0.f; }
-      tmem_st8(cRhi + lane + c0 + 8 * j, v);
-      tmem_st8(cRlo + lane + c0 + 8 * j, z);
-    }
-    tmem_wait_st();
-  }
-
-  uint32_t ph_mma = 0, ph_a0 = 0, ph_a1 = 0;
-  bool bad = false;
-  const float x1 = kT8tc[0], x2 = kT8tc[1], x3 = kT8tc[2], x4 = kT8tc[3], x5 = kT8tc[4],
-              x6 = kT8tc[5], x7 = kT8tc[6], y2 = kT8tc[7];
-
-  for (int t = t0; t < t1; ++t) {
-    const int sidx = (t - t0) & 1;
-    const float* av = stage0 + sidx * (L::kStage / 4);
-    if (__syncthreads_or(bad)) { bad = true; break; }
-    // prefetch the next edge's generator into the other stage (its readers are done)
-    if (tid == 0 && t + 1 < t1) {
-      fence_proxy_async_smem();
-      float* nxt = stage0 + (sidx ^ 1) * (L::kStage / 4);
-      mbar_arrive_expect_tx(&bar_a[sidx ^ 1], m * 4);
-      bulk_load(nxt, gen_ptr(t + 1), m * 4, &bar_a[sidx ^ 1]);
-    }
-    if (t + 1 < t1) load_vec(t + 1);
-    if (sidx == 0) { bad |= !mbar_wait(&bar_a[0], ph_a0); ph_a0 ^= 1; }
-    else { bad |= !mbar_wait(&bar_a[1], ph_a1); ph_a1 ^= 1; }
-
-    // ---- P1: A -> TMEM (fp32) and X rows; D1 = A A^T = -A^2 ---------------------
+  // A rows (this thread's columns) from stage s -> TMEM (fp32) and X (tf32 hi, lo)
+  auto build_a = [&](int s) {
+    const float* av = stage_gen(s);
 #pragma unroll
     for (int j = 0; j < NCH; ++j) {
       float v[8];
@@ -281,26 +264,72 @@ __global__ void __launch_bounds__(LtLayout<DP>::NT, 1) link_tc_kernel(LinkTcArgs
       if (row_ok) put_row8<DP>(Xhi, Xlo, r, c0 + 8 * j, v);
     }
     tmem_wait_st();
-    operand_barrier();
-    if (tid == 0 && !bad) {
-      issue_ss<DP>(cD1, sXhi, sXlo, sXhi, sXlo);
-      tc_commit(bar_mma);
+  };
+
+  bool bad = false;
+  uint32_t ph_mma = 0, ph_p1 = 0, ph_a0 = 0, ph_a1 = 0;
+  auto wait_stage = [&](int s) {
+    if (s == 0) { bad |= !mbar_wait(&bar_a[0], ph_a0); ph_a0 ^= 1; }
+    else { bad |= !mbar_wait(&bar_a[1], ph_a1); ph_a1 ^= 1; }
+  };
+
+  // ---- prologue: position t0 (R = I, U = (q, k, v)), A(t0), and P1(t0) -> D2
+  if (tid == 0) fetch(0, t0);
+  wait_stage(0);
+  add_bias(0);
+  __syncthreads();
+  {
+    const long long pos = (long long)chain * p.T + t0;
+    float* Rg = p.R + pos * DP * DP;
+    for (int i = tid; i < DP * DP; i += NT) Rg[i] = (i / DP == i % DP) ? 1.f : 0.f;
+    float* Ug = p.U + pos * 3 * DP;
+    const uint8_t* qv = stage_qkv(0);
+    for (int i = tid; i < 3 * DP; i += NT) Ug[i] = load_elem(qv, i, p.qkv_dtype);
+#pragma unroll
+    for (int j = 0; j < NCH; ++j) {
+      float v[8], z[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) { v[i] = (c0 + 8 * j + i == r) ? 1.f : 0.f; z[i] = 0.f; }
+      tmem_st8(cRhi + lane + c0 + 8 * j, v);
+      tmem_st8(cRlo + lane + c0 + 8 * j, z);
     }
-    bad |= !mbar_wait(bar_mma, ph_mma);
-    ph_mma ^= 1;
-    tc_fence_after();
+  }
+  build_a(0);
+  operand_barrier();
+  if (tid == 0 && !bad) {
+    issue_ss<DP>(cD2, sXhi, sXlo, sXhi, sXlo);      // D = A A^T = -A^2
+    tc_commit(bar_p1);
+  }
+
+  const float x1 = kT8tc[0], x2 = kT8tc[1], x3 = kT8tc[2], x4 = kT8tc[3], x5 = kT8tc[4],
+              x6 = kT8tc[5], x7 = kT8tc[6], y2 = kT8tc[7];
+
+  for (int t = t0; t < t1; ++t) {
+    const int it = t - t0;
+    const int sidx = it & 1;
+    // TMEM roles alternate: P holds P1(t) = -A^2, Q the other accumulator
+    const uint32_t cP = sidx ? cD1 : cD2, cQ = sidx ? cD2 : cD1;
+    const bool last = (t + 1 == t1);
+    if (__syncthreads_or(bad)) { bad = true; break; }
+    if (tid == 0 && !last) {                 // stage sidx^1 was last read two positions ago
+      fence_proxy_async_smem();
+      fetch(sidx ^ 1, t + 1);
+    }
 
     // ---- theta^2 = ||A^2||_1 (A^2 symmetric: max row abs-sum) ---------------
+    bad |= !mbar_wait(bar_p1, ph_p1);
+    ph_p1 ^= 1;
+    tc_fence_after();
     {
+      float v[NCH][8];
+#pragma unroll
+      for (int j = 0; j < NCH; ++j) tmem_ld8(cP + lane + c0 + 8 * j, v[j]);
+      tmem_wait_ld();
       float rs = 0.f;
 #pragma unroll
-      for (int j = 0; j < NCH; ++j) {
-        float v[8];
-        tmem_ld8(cD1 + lane + c0 + 8 * j, v);
-        tmem_wait_ld();
+      for (int j = 0; j < NCH; ++j)
 #pragma unroll
-        for (int i = 0; i < 8; ++i) rs += fabsf(v[i]);
-      }
+        for (int i = 0; i < 8; ++i) rs += fabsf(v[j][i]);
       XT[q * 128 + r] = row_ok ? rs : 0.f;
       __syncthreads();
       if (q == 0) {
@@ -319,13 +348,13 @@ __global__ void __launch_bounds__(LtLayout<DP>::NT, 1) link_tc_kernel(LinkTcArgs
       while (theta > kTheta8tc && nsq < 64) { theta *= 0.5f; ++nsq; }
     }
     const float sa = ldexpf(1.f, -nsq);
-    const float sa2 = -ldexpf(1.f, -2 * nsq);    // A2s = -D1 * 4^-s
+    const float sa2 = -ldexpf(1.f, -2 * nsq);    // A2s = -P * 4^-s
 
-    // ---- P2: X = A2s rows, Y^T = T1^T = -x1 As + x2 A2s rows; D2 = A4 ------------
+    // ---- P2: X = A2s rows, Y^T = T1^T = -x1 As + x2 A2s rows; Q = A4 -------------
 #pragma unroll
     for (int j = 0; j < NCH; ++j) {
       float a2[8], a[8];
-      tmem_ld8(cD1 + lane + c0 + 8 * j, a2);
+      tmem_ld8(cP + lane + c0 + 8 * j, a2);
       tmem_ld8(cA + lane + c0 + 8 * j, a);
       tmem_wait_ld();
       if (row_ok) {
@@ -341,7 +370,7 @@ __global__ void __launch_bounds__(LtLayout<DP>::NT, 1) link_tc_kernel(LinkTcArgs
     }
     operand_barrier();
     if (tid == 0 && !bad) {
-      issue_ss<DP>(cD2, sXhi, sXlo, sYhi, sYlo);
+      issue_ss<DP>(cQ, sXhi, sXlo, sYhi, sYlo);
       tc_commit(bar_mma);
     }
     bad |= !mbar_wait(bar_mma, ph_mma);
@@ -349,24 +378,26 @@ __global__ void __launch_bounds__(LtLayout<DP>::NT, 1) link_tc_kernel(LinkTcArgs
     tc_fence_after();
 
     // ---- A4 -> transpose scratch, so that each thread can read its part of A4^T
+    {
+      float a4[NCH][8];
 #pragma unroll
-    for (int j = 0; j < NCH; ++j) {
-      float a4[8];
-      tmem_ld8(cD2 + lane + c0 + 8 * j, a4);
+      for (int j = 0; j < NCH; ++j) tmem_ld8(cQ + lane + c0 + 8 * j, a4[j]);
       tmem_wait_ld();
       if (row_ok) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) XT[r * (DP + 1) + c0 + 8 * j + i] = a4[i];
+        for (int j = 0; j < NCH; ++j)
+#pragma unroll
+          for (int i = 0; i < 8; ++i) XT[r * (DP + 1) + c0 + 8 * j + i] = a4[j][i];
       }
     }
     __syncthreads();
 
-    // ---- P3: X = L rows, Y^T = F^T rows; N0 = As + (y2 + x3 x4) A2s + x4 A4 -> D1
+    // ---- P3: X = L rows, Y^T = F^T rows; N0 = As + (y2 + x3 x4) A2s + x4 A4 -> P
 #pragma unroll
     for (int j = 0; j < NCH; ++j) {
       float a2[8], a4[8], a[8], n0[8];
-      tmem_ld8(cD1 + lane + c0 + 8 * j, a2);
-      tmem_ld8(cD2 + lane + c0 + 8 * j, a4);
+      tmem_ld8(cP + lane + c0 + 8 * j, a2);
+      tmem_ld8(cQ + lane + c0 + 8 * j, a4);
       tmem_ld8(cA + lane + c0 + 8 * j, a);
       tmem_wait_ld();
       if (row_ok) {
@@ -387,24 +418,24 @@ __global__ void __launch_bounds__(LtLayout<DP>::NT, 1) link_tc_kernel(LinkTcArgs
 #pragma unroll
         for (int i = 0; i < 8; ++i) n0[i] = 0.f;
       }
-      tmem_st8(cD1 + lane + c0 + 8 * j, n0);
+      tmem_st8(cP + lane + c0 + 8 * j, n0);
     }
     tmem_wait_st();
     operand_barrier();
     if (tid == 0 && !bad) {
-      issue_ss<DP>(cD2, sXhi, sXlo, sYhi, sYlo);        // D2 = L F
+      issue_ss<DP>(cQ, sXhi, sXlo, sYhi, sYlo);        // Q = L F
       tc_commit(bar_mma);
     }
     bad |= !mbar_wait(bar_mma, ph_mma);
     ph_mma ^= 1;
     tc_fence_after();
 
-    // ---- N = G - I = N0 + D2, then s squarings N <- 2N + N N; N rows -> Y -------
+    // ---- N = G - I = N0 + L F, then s squarings N <- 2N + N N; N rows -> Y ------
 #pragma unroll
     for (int j = 0; j < NCH; ++j) {
       float n0[8], nv[8];
-      tmem_ld8(cD1 + lane + c0 + 8 * j, n0);
-      tmem_ld8(cD2 + lane + c0 + 8 * j, nv);
+      tmem_ld8(cP + lane + c0 + 8 * j, n0);
+      tmem_ld8(cQ + lane + c0 + 8 * j, nv);
       tmem_wait_ld();
       if (row_ok) {
 #pragma unroll
@@ -434,7 +465,7 @@ __global__ void __launch_bounds__(LtLayout<DP>::NT, 1) link_tc_kernel(LinkTcArgs
       }
       operand_barrier();
       if (tid == 0 && !bad) {
-        issue_ss<DP>(cD2, sXhi, sXlo, sYhi, sYlo);
+        issue_ss<DP>(cQ, sXhi, sXlo, sYhi, sYlo);
         tc_commit(bar_mma);
       }
       bad |= !mbar_wait(bar_mma, ph_mma);
@@ -443,7 +474,7 @@ __global__ void __launch_bounds__(LtLayout<DP>::NT, 1) link_tc_kernel(LinkTcArgs
 #pragma unroll
       for (int j = 0; j < NCH; ++j) {
         float nv[8];
-        tmem_ld8(cD2 + lane + c0 + 8 * j, nv);
+        tmem_ld8(cQ + lane + c0 + 8 * j, nv);
         tmem_wait_ld();
         if (row_ok) {
 #pragma unroll
@@ -459,27 +490,40 @@ __global__ void __launch_bounds__(LtLayout<DP>::NT, 1) link_tc_kernel(LinkTcArgs
     }
     operand_barrier();
 
-    // ---- P4: D1 = R^T N^T ------------------------------------------------------
+    // ---- P4: P = R^T N^T (issued; its readout overlaps the next position's P1)
     if (tid == 0 && !bad) {
-      issue_ts<DP>(cD1, cRhi, cRlo, sYhi, sYlo);
+      issue_ts<DP>(cP, cRhi, cRlo, sYhi, sYlo);
       tc_commit(bar_mma);
     }
+
+    // ---- next position: A(t+1) -> X and TMEM, P1(t+1) -> Q (queued behind P4)
+    if (!last) {
+      wait_stage(sidx ^ 1);
+      add_bias(sidx ^ 1);
+      __syncthreads();
+      build_a(sidx ^ 1);
+      operand_barrier();
+      if (tid == 0 && !bad) {
+        issue_ss<DP>(cQ, sXhi, sXlo, sXhi, sXlo);
+        tc_commit(bar_p1);
+      }
+    }
+
+    // ---- R_{t+1}^T = R^T + P (R^T = hi + lo exactly); write R_{t+1} and U_{t+1},
+    //      or the chunk total after the chunk's last edge.
     bad |= !mbar_wait(bar_mma, ph_mma);
     ph_mma ^= 1;
     tc_fence_after();
-
-    // ---- R_{t+1}^T = R^T + D1 (R^T = hi + lo exactly); write R_{t+1}, U_{t+1},
-    //      or the chunk total after the chunk's last edge.
-    const bool last = (t + 1 == t1);
     const long long pos1 = (long long)chain * p.T + t + 1;
     float* Rg = last ? p.M + ((long long)chain * p.K + kc) * DP * DP : p.R + pos1 * DP * DP;
+    const uint8_t* qv = stage_qkv(sidx ^ 1);
     float u0 = 0.f, u1 = 0.f, u2 = 0.f;
 #pragma unroll
     for (int j = 0; j < NCH; ++j) {
       float rh[8], rl[8], dv[8];
       tmem_ld8(cRhi + lane + c0 + 8 * j, rh);
       tmem_ld8(cRlo + lane + c0 + 8 * j, rl);
-      tmem_ld8(cD1 + lane + c0 + 8 * j, dv);
+      tmem_ld8(cP + lane + c0 + 8 * j, dv);
       tmem_wait_ld();
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
@@ -495,9 +539,11 @@ __global__ void __launch_bounds__(LtLayout<DP>::NT, 1) link_tc_kernel(LinkTcArgs
         for (int i = 0; i < 8; ++i) {
           const int k = c0 + 8 * j + i;                 // dv[i] = R_{t+1}[k][r]
           Rg[(long long)k * DP + r] = dv[i];
-          u0 = fmaf(dv[i], svec[k], u0);
-          u1 = fmaf(dv[i], svec[DP + k], u1);
-          u2 = fmaf(dv[i], svec[2 * DP + k], u2);
+          if (!last) {
+            u0 = fmaf(dv[i], load_elem(qv, k, p.qkv_dtype), u0);
+            u1 = fmaf(dv[i], load_elem(qv, DP + k, p.qkv_dtype), u1);
+            u2 = fmaf(dv[i], load_elem(qv, 2 * DP + k, p.qkv_dtype), u2);
+          }
         }
       }
     }
@@ -543,12 +589,13 @@ int launch_link_tc(const LinkTcArgs& a, cudaStream_t s) {
 
 // Entry used by hoa_link_local: returns HOA_ERR_UNSUPPORTED when this variant
 // does not serve the shape (the caller then runs the SIMT kernel).
-int link_local_tc(const void* a_all, int a_dtype, float edge_scale, const void* qkv,
+int link_local_tc(const void* a_all, int a_dtype, const float* a_bias, float edge_scale, const void* qkv,
                   int qkv_dtype, float* R, float* U, float* M, int* status, int B, int H, int T,
                   int d, int chunk, cudaStream_t s) {
-  if (a_dtype != HOA_F32 || (reinterpret_cast<uintptr_t>(a_all) & 15) != 0)
+  if (a_dtype != HOA_F32 || (reinterpret_cast<uintptr_t>(a_all) & 15) != 0 ||
+      (reinterpret_cast<uintptr_t>(qkv) & 15) != 0)
     return HOA_ERR_UNSUPPORTED;
-  LinkTcArgs a{static_cast<const float*>(a_all), edge_scale, qkv, qkv_dtype, R, U, M, status,
+  LinkTcArgs a{static_cast<const float*>(a_all), a_bias, edge_scale, qkv, qkv_dtype, R, U, M, status,
                B, H, T, chunk, ceil_div(T, chunk)};
   switch (d) {
     case 32: return launch_link_tc<32>(a, s);

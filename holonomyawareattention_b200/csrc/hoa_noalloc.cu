@@ -46,7 +46,8 @@ int noalloc_scratch(void** out) {
 }
 }  // namespace
 
-extern "C" int hoa_core_forward_noalloc(const void* a_all, int a_dtype, float edge_scale,
+extern "C" int hoa_core_forward_noalloc(const void* a_all, int a_dtype, const float* a_bias,
+                                        float edge_scale,
                                         const void* qkv, int qkv_dtype, void* out, int out_dtype,
                                         int hat_dtype, float softmax_scale, const float* carry_in,
                                         float* total_out, int B, int H, int T, int d, int chunk,
@@ -59,7 +60,7 @@ extern "C" int hoa_core_forward_noalloc(const void* a_all, int a_dtype, float ed
   void* scratch = nullptr;
   const int st = noalloc_scratch(&scratch);
   if (st != HOA_OK) return st;
-  return hoa_core_forward(a_all, a_dtype, edge_scale, qkv, qkv_dtype, out, out_dtype, hat_dtype,
+  return hoa_core_forward(a_all, a_dtype, a_bias, edge_scale, qkv, qkv_dtype, out, out_dtype, hat_dtype,
                           softmax_scale, carry_in, total_out, B, H, T, d, chunk, scratch,
                           (size_t)HOA_NOALLOC_SCRATCH_BYTES, stream);
 }

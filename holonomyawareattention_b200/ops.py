@@ -54,14 +54,16 @@ def core_forward(a_all: torch.Tensor, qkv: torch.Tensor, n_heads: int, edge_scal
                  softmax_scale: Optional[float] = None, out_dtype: Optional[torch.dtype] = None,
                  hat_dtype: Optional[torch.dtype] = None, chunk: Optional[int] = None,
                  carry_in: Optional[torch.Tensor] = None,
-                 total_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+                 total_out: Optional[torch.Tensor] = None,
+                 a_bias: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Core region (kernels 1-4): a_all (B,T,H*m) and qkv (B,T,3D) -> heads (B,T,D).
 
     ``a_all`` is the raw edge-MLP output (edge_scale is applied in the kernel,
-    as core/attention_fast_chunked.py:77 does).  ``carry_in`` / ``total_out``
+    as core/attention_fast_chunked.py:77 does); ``a_bias`` (H*m, fp32) is the
+    MLP's output bias when the GEMM left it out.  ``carry_in`` / ``total_out``
     are optional (B*H, d, d) fp32 tensors (see hoa_core_forward).
     """
-    _need_cuda(a_all, qkv, carry_in, total_out)
+    _need_cuda(a_all, qkv, carry_in, total_out, a_bias)
     B, T, threeD = qkv.shape
     D = threeD // 3
     H = n_heads
@@ -72,6 +74,7 @@ def core_forward(a_all: torch.Tensor, qkv: torch.Tensor, n_heads: int, edge_scal
     _contig(a_all, "a_all"); _contig(qkv, "qkv")
     if softmax_scale is None:
         softmax_scale = 1.0 / math.sqrt(d)
+    _check_bias(a_bias, H * m)
     out_dtype = out_dtype or qkv.dtype
     hat_dtype = hat_dtype or qkv.dtype
     if chunk is None:
@@ -84,7 +87,7 @@ def core_forward(a_all: torch.Tensor, qkv: torch.Tensor, n_heads: int, edge_scal
     ws_bytes = int(lib.hoa_core_workspace_bytes(B, H, T, d, chunk, hat_code))
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=qkv.device)
     out = torch.empty(B, T, D, dtype=out_dtype, device=qkv.device)
-    _lib.call("hoa_core_forward", _ptr(a_all), _dtype_code(a_all.dtype), float(edge_scale),
+    _lib.call("hoa_core_forward", _ptr(a_all), _dtype_code(a_all.dtype), _ptr(a_bias), float(edge_scale),
               _ptr(qkv), _dtype_code(qkv.dtype), _ptr(out), _dtype_code(out_dtype), hat_code,
               float(softmax_scale), _ptr(carry_in), _ptr(total_out), B, H, T, d, int(chunk),
               _ptr(ws), ws_bytes, _stream(qkv.device))
@@ -94,20 +97,28 @@ def core_forward(a_all: torch.Tensor, qkv: torch.Tensor, n_heads: int, edge_scal
 # ---------------------------------------------------------------------------
 # individual stages (used by the tests and by the sequence-sharded path)
 # ---------------------------------------------------------------------------
+def _check_bias(a_bias, n):
+    if a_bias is not None and (a_bias.dtype != torch.float32 or a_bias.numel() != n
+                               or not a_bias.is_contiguous()):
+        raise ValueError(f"a_bias must be a contiguous fp32 tensor of {n} elements")
+
+
 def link_local(a_all: torch.Tensor, qkv: torch.Tensor, n_heads: int, edge_scale: float,
-               chunk: int) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+               chunk: int, a_bias: Optional[torch.Tensor] = None
+               ) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
     """Kernel (1)+(2) local part -> (R (BH,T,d,d), U (BH,T,3,d), M (BH,K,d,d)), all fp32."""
-    _need_cuda(a_all, qkv)
+    _need_cuda(a_all, qkv, a_bias)
     B, T, threeD = qkv.shape
     H = n_heads
     d = threeD // 3 // H
     K = (T + chunk - 1) // chunk
     _contig(a_all, "a_all"); _contig(qkv, "qkv")
+    _check_bias(a_bias, H * d * (d - 1) // 2)
     dev = qkv.device
     R = torch.empty(B * H, T, d, d, dtype=torch.float32, device=dev)
     U = torch.empty(B * H, T, 3, d, dtype=torch.float32, device=dev)
     M = torch.empty(B * H, K, d, d, dtype=torch.float32, device=dev)
-    _lib.call("hoa_link_local", _ptr(a_all), _dtype_code(a_all.dtype), float(edge_scale), _ptr(qkv),
+    _lib.call("hoa_link_local", _ptr(a_all), _dtype_code(a_all.dtype), _ptr(a_bias), float(edge_scale), _ptr(qkv),
               _dtype_code(qkv.dtype), _ptr(R), _ptr(U), _ptr(M), B, H, T, d, int(chunk),
               _stream(dev))
     return R, U, M
@@ -186,12 +197,13 @@ def uses_tensor_cores(hat_dtype: torch.dtype, d: int) -> bool:
     return hat_dtype == torch.bfloat16 and d % 8 == 0 and d <= 128
 
 
-def core_stages(a_all, qkv, n_heads, edge_scale, softmax_scale, out_dtype, hat_dtype, chunk):
+def core_stages(a_all, qkv, n_heads, edge_scale, softmax_scale, out_dtype, hat_dtype, chunk,
+                a_bias=None):
     """The core region as separate stage calls (same kernels as core_forward)."""
     B, T, threeD = qkv.shape
     H = n_heads
     d = threeD // 3 // H
-    R, U, M = link_local(a_all, qkv, H, edge_scale, chunk)
+    R, U, M = link_local(a_all, qkv, H, edge_scale, chunk, a_bias)
     C, _ = carry_scan(M)
     tc = uses_tensor_cores(hat_dtype, d)
     qh, kh, vh = carry_apply(U, C, chunk, hat_dtype, v_transposed=tc)

@@ -65,7 +65,10 @@ size_t hoa_core_workspace_bytes(int B, int H, int T, int d, int chunk, int hat_d
  *   core/attention_fast_chunked.py:108-110 transport q^, k^, v^
  *   core/attention_fast_chunked.py:119-171 causal fold and out_i = P_i o_i
  * (kernel/attention_kernel.py:215-216 `_geometry` + `HoloAttnFn.apply`).
- * a_dtype / qkv_dtype / out_dtype: HOA_F32 or HOA_BF16.  hat_dtype is the
+ * a_dtype / qkv_dtype / out_dtype: HOA_F32 or HOA_BF16.  `a_bias` (nullable,
+ * (H*m) fp32) is added to every generator before the edge_scale multiply — the
+ * edge MLP's output bias, so that the projection GEMM may leave it out
+ * (core/attention_fast_chunked.py:76-77).  hat_dtype is the
  * dtype of the transported q^/k^/v^ fed to attention: HOA_BF16 runs the
  * tcgen05 tensor-core attention (d % 8 == 0, d <= 128), HOA_F32 the fp32 SIMT
  * attention.  `carry_in` (nullable, (B*H, d, d) fp32) is P at the first
@@ -74,7 +77,7 @@ size_t hoa_core_workspace_bytes(int B, int H, int T, int d, int chunk, int hat_d
  * t = T-1 (for a full sequence that edge is the closing edge, and total_out
  * is the holonomy G_close P_{T-1}, core/attention_fast_chunked.py:95).
  */
-int hoa_core_forward(const void* a_all, int a_dtype, float edge_scale,
+int hoa_core_forward(const void* a_all, int a_dtype, const float* a_bias, float edge_scale,
                      const void* qkv, int qkv_dtype,
                      void* out, int out_dtype, int hat_dtype, float softmax_scale,
                      const float* carry_in, float* total_out,
@@ -91,7 +94,7 @@ int hoa_core_forward(const void* a_all, int a_dtype, float edge_scale,
  * Replaces core/attention_fast_chunked.py:86-94 (with core/utils.py:4-52)
  * and the transport at :108-110, split into independent chunks.
  */
-int hoa_link_local(const void* a_all, int a_dtype, float edge_scale,
+int hoa_link_local(const void* a_all, int a_dtype, const float* a_bias, float edge_scale,
                    const void* qkv, int qkv_dtype,
                    float* R, float* U, float* M,
                    int B, int H, int T, int d, int chunk, void* stream);
@@ -165,7 +168,8 @@ int hoa_out_transport(const float* o, const float* R, const float* C, int chunk,
  * contents: calls that overlap on the GPU (other streams, other host
  * threads) race on it, so serialise them.
  */
-int hoa_core_forward_noalloc(const void* a_all, int a_dtype, float edge_scale,
+int hoa_core_forward_noalloc(const void* a_all, int a_dtype, const float* a_bias,
+                             float edge_scale,
                              const void* qkv, int qkv_dtype,
                              void* out, int out_dtype, int hat_dtype, float softmax_scale,
                              const float* carry_in, float* total_out,

@@ -36,7 +36,7 @@ def _inputs(seed, B, T, H, d, dtype):
 def _noalloc(lib, a, qkv, H, d, es, chunk, dtype, out):
     B, T, _ = qkv.shape
     code = 0 if dtype == torch.float32 else 1
-    return lib.hoa_core_forward_noalloc(a.data_ptr(), 0, es, qkv.data_ptr(), code, out.data_ptr(),
+    return lib.hoa_core_forward_noalloc(a.data_ptr(), 0, None, es, qkv.data_ptr(), code, out.data_ptr(),
                                         code, code, 1.0 / math.sqrt(d), None, None, B, H, T, d,
                                         chunk, torch.cuda.current_stream().cuda_stream)
 
@@ -63,7 +63,7 @@ def test_noalloc_rejects_problems_beyond_its_scratch():
     assert lib.hoa_core_workspace_bytes(B, H, T, d, chunk, 0) > 16 * 1024 * 1024
     a, qkv = _inputs(3, 1, 4, H, d, torch.float32)      # pointers only; nothing is launched
     out = torch.empty(1, dtype=torch.float32, device=DEV)
-    st = lib.hoa_core_forward_noalloc(a.data_ptr(), 0, 0.3, qkv.data_ptr(), 0, out.data_ptr(), 0, 0,
+    st = lib.hoa_core_forward_noalloc(a.data_ptr(), 0, None, 0.3, qkv.data_ptr(), 0, out.data_ptr(), 0, 0,
                                       0.1, None, None, B, H, T, d, chunk,
                                       torch.cuda.current_stream().cuda_stream)
     assert st == 4                                       # HOA_ERR_WORKSPACE
