@@ -39,7 +39,10 @@ CONFIGS = {
     "c4slice": (16, 2048, 2880, 24, "bf16"),
     # small case of the c3 kernels for ncu captures (inputs still larger than L2)
     "c3prof": (1, 512, 1536, 16, "bf16"),
+    # one sequence of T=65536 split across the ranks (sequence sharding)
+    "c5": (1, 65536, 1536, 16, "bf16"),
 }
+SEQ_SHARDED = {"c5"}
 EDGE_SCALE = 0.05
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
 
@@ -182,6 +185,13 @@ def run_reference_arm(args):
 
 def config_obj(name, n):
     B, T, D, H, dt = CONFIGS[name]
+    if name in SEQ_SHARDED:
+        return {"workload": f"{name}: B={B}, T={T} split into {n} sequence shards, d_model={D}, "
+                            f"H={H}, head_dim={D // H}, {dt} activations, fp32 rotations, "
+                            f"edge_scale {EDGE_SCALE}",
+                "global_batch": B, "seq_len": T, "d_model": D, "heads": H, "head_dim": D // H,
+                "parallelism": f"sequence-sharded x{n} (NCCL all-gather of shard totals and K/V)",
+                "l2": "inputs and workspace (tens of GB) far exceed the 126 MB L2"}
     return {"workload": f"{name}: B={B}/GPU, T={T}, d_model={D}, H={H}, head_dim={D // H}, {dt} "
                         f"activations, fp32 rotations, edge_scale {EDGE_SCALE}",
             "global_batch": B * n, "seq_len": T, "d_model": D, "heads": H, "head_dim": D // H,
@@ -369,6 +379,121 @@ def run_ours(args):
     return 0
 
 
+def run_seq_sharded(args):
+    """one long sequence split into contiguous shards, one per rank
+    (sequence sharding: NCCL all-gather of the shard totals and of K/V).
+    Strong scaling: the total work is fixed; value = B*T / time."""
+    import socket
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    from datetime import timedelta
+    if world == 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        if "MASTER_PORT" not in os.environ:
+            with socket.socket() as s:
+                s.bind(("127.0.0.1", 0))
+                os.environ["MASTER_PORT"] = str(s.getsockname()[1])
+        dist.init_process_group("nccl", rank=0, world_size=1, timeout=timedelta(seconds=600),
+                                device_id=dev)
+    else:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
+    from holonomyawareattention_b200 import PathOrderedGeometricMHA, seqshard
+
+    B, T, D, H, dtn = CONFIGS[args.config]
+    dtype = torch.bfloat16 if dtn == "bf16" else torch.float32
+    d = D // H
+    torch.manual_seed(0)
+    with torch.device(dev):
+        mod = PathOrderedGeometricMHA(D, n_heads=H, edge_scale=EDGE_SCALE)
+    mod = mod.to(dtype).eval()
+    g = torch.Generator(device=dev).manual_seed(1000)
+    x = torch.randn(B, T, D, device=dev, generator=g).to(dtype)       # same sequence on every rank
+    s0, s1 = seqshard.shard_range(T, world, rank)
+    xs = x[:, s0:s1].contiguous()
+    del x
+    stream = torch.cuda.current_stream(dev)
+    clocks = ClockSampler(physical_gpu_index(local))
+    with torch.inference_mode():
+        for _ in range(args.warmup):
+            seqshard.sequence_sharded_forward(mod, xs)
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        torch.cuda.synchronize(dev)
+        clocks.start()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            y = seqshard.sequence_sharded_forward(mod, xs)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        clk = clocks.stop()
+        dist.barrier()
+        t = torch.tensor([e0.elapsed_time(e1) / args.steps], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        # end to end: the shard's input from pinned host memory, its output back
+        xh = xs.cpu().pin_memory()
+        yh = torch.empty(tuple(y.shape), dtype=y.dtype).pin_memory()
+        xd = torch.empty_like(xs)
+        dist.barrier()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for _ in range(args.steps):
+            xd.copy_(xh, non_blocking=True)
+            yy = seqshard.sequence_sharded_forward(mod, xd)
+            yh.copy_(yy, non_blocking=True)
+        f1.record(stream)
+        torch.cuda.synchronize(dev)
+        t2 = torch.tensor([f0.elapsed_time(f1) / args.steps], dtype=torch.float64, device=dev)
+        dist.all_reduce(t2, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t2.item())
+    peaks = load_peaks()
+    n_pos = B * H * T
+    m_dim = d * (d - 1) // 2
+    core_bytes = n_pos * (m_dim * 4 + 4 * d * 2)
+    f_attn = 4.0 * B * H * d * T * (T + 1) / 2
+    bf16_peak = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
+    roof_s = max(f_attn / (bf16_peak * 1e12 * world), core_bytes / (peaks["hbm_gbs"] * 1e9 * world))
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        p = seeded_params_np(D, H)
+        Ts = cpu_sample_len(T)
+        cpu_sample_forward(p, D, H, min(Ts, 32))
+        sec = cpu_sample_forward(p, D, H, Ts)
+        cpu = {"value": Ts / sec, "unit": "tokens/s", "cores": cpu_threads(), "kind": "port",
+               "sample": f"1 sequence of T={Ts} at d_model={D}, H={H} (numpy float32 restatement "
+                         "of the reference forward, bf16-valued inputs/weights)"}
+    line = {
+        "metric": METRIC, "value": B * T / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16" if dtype == torch.bfloat16 else "f32",
+        "data": "synthetic (x ~ N(0,1), seeded default-init weights)",
+        "config": config_obj(args.config, world),
+        "per_gpu_tokens_s": B * T / (ms / 1e3) / world,
+        "roofline": {"bound": "hbm", "kernel": "whole sharded forward",
+                     "achieved": core_bytes / world / (ms / 1e3) / 1e9, "peak": peaks["hbm_gbs"],
+                     "unit": "GB/s", "frac": core_bytes / world / (ms / 1e3) / 1e9 / peaks["hbm_gbs"],
+                     "traffic": None, "peak_source": f"{peaks['source']} hbm_gbs (of {peaks['source']})"},
+        "roofline_baseline_formula": {"target_ms": roof_s * 1e3, "ms": ms, "frac": roof_s * 1e3 / ms},
+        "cpu_baseline": cpu,
+        "e2e": {"value": B * T / (e2e_ms / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": xs.numel() * xs.element_size(),
+                "d2h_bytes_per_step": xs.numel() * xs.element_size()},
+        "gpu_launches": 6 * args.steps, "clocks": clk,
+        "generator_precision": mod.generator_precision,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -385,6 +510,8 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         return run_reference_arm(args)
+    if args.config in SEQ_SHARDED:
+        return run_seq_sharded(args)
     return run_ours(args)
 
 

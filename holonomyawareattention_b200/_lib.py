@@ -34,9 +34,9 @@ SIGNATURES = {
                                 c_int, c_int, c_int, c_int, c_void_p]),
     "hoa_vt_stride": (c_int, [c_int]),
     "hoa_attn_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_float, c_int, c_int,
-                             c_int, c_void_p]),
+                             c_int, c_int, c_int, c_void_p]),
     "hoa_attn_tc_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_int,
-                                c_int, c_int, c_void_p]),
+                                c_int, c_int, c_int, c_int, c_void_p]),
     "hoa_out_transport": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_int,
                                   c_int, c_int, c_int, c_void_p]),
     "hoa_core_forward_noalloc": (c_int, [c_void_p, c_int, c_void_p, c_float, c_void_p, c_int, c_void_p, c_int,

@@ -127,12 +127,21 @@ class PathOrderedGeometricMHA(nn.Module):
         a, bias = self._edge_generators_nobias(x)
         return a if bias is None else a + bias
 
-    def _edge_generators_nobias(self, x: torch.Tensor):
+    def _edge_generators_nobias(self, x: torch.Tensor, x_next: Optional[torch.Tensor] = None):
         """(a_all without the MLP's output bias, that bias or None): the link
         kernel adds the bias while it stages each generator, so the large fp32
-        output is written once by the GEMM and never touched again."""
+        output is written once by the GEMM and never touched again.
+
+        ``x_next`` (B, 1, D), for a sequence shard: the token that follows the
+        shard (the next shard's first token; the whole sequence's first token
+        for the last shard, as the reference's roll wraps).  None: ``x`` is the
+        whole sequence and the pair partner is roll(x, -1)."""
         B, L, D = x.shape
-        pair = torch.cat([x, torch.roll(x, shifts=-1, dims=1)], dim=-1)
+        if x_next is None:
+            partner = torch.roll(x, shifts=-1, dims=1)
+        else:
+            partner = torch.cat([x[:, 1:], x_next.to(x.dtype)], dim=1)
+        pair = torch.cat([x, partner], dim=-1)
         lin0, lin2 = self.edge_mlp[0], self.edge_mlp[2]
         if x.dtype == torch.float32:
             return self.edge_mlp(pair), None

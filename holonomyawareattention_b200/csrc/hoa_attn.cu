@@ -25,7 +25,7 @@ template <int DA> struct AttnCfg {
 struct AttnArgs {
   const void* qh; const void* kh; const void* vh; int hat_dtype;
   float* o; float scale;
-  int T, d;
+  int Tq, Tk, q_offset, d;   // query rows are global positions q_offset .. q_offset + Tq - 1
 };
 
 template <int N>
@@ -63,15 +63,18 @@ __global__ void __launch_bounds__(kAttnThreads) attn_fwd_simt_kernel(AttnArgs p)
   const int r0 = ty * 4, c0 = tx * 4;
   const int chain = blockIdx.y;
   const int qtile = gridDim.x - 1 - blockIdx.x;     // heaviest causal tiles first
-  const int q0 = qtile * kBQ;
-  const int d = p.d, T = p.T;
-  const long long base = (long long)chain * T * d;
+  const int q0 = qtile * kBQ;                        // local row of this tile
+  const int d = p.d, Tq = p.Tq, Tk = p.Tk;
+  const int gq0 = p.q_offset + q0;                   // its global position
+  const int nkt = min((gq0 + kBQ - 1) / kBK, (Tk - 1) / kBK) + 1;
+  const long long qbase = (long long)chain * Tq * d;
+  const long long kbase = (long long)chain * Tk * d;
 
   for (int i = tid; i < kBQ * DA; i += kAttnThreads) {
     const int r = i / DA, e = i % DA;
     const int t = q0 + r;
-    Qt[e * kLDT + r] = (t < T && e < d) ? load_elem(p.qh, base + (long long)t * d + e, p.hat_dtype)
-                                        : 0.f;
+    Qt[e * kLDT + r] = (t < Tq && e < d) ? load_elem(p.qh, qbase + (long long)t * d + e, p.hat_dtype)
+                                         : 0.f;
   }
 
   float mrow[4], lrow[4], o[4][CPT];
@@ -83,14 +86,14 @@ __global__ void __launch_bounds__(kAttnThreads) attn_fwd_simt_kernel(AttnArgs p)
     for (int j = 0; j < CPT; ++j) o[i][j] = 0.f;
   }
 
-  for (int kt = 0; kt <= qtile; ++kt) {
+  for (int kt = 0; kt < nkt; ++kt) {
     const int k0 = kt * kBK;
     __syncthreads();
     for (int i = tid; i < kBK * DA; i += kAttnThreads) {
       const int r = i / DA, e = i % DA;
       const int t = k0 + r;
-      const bool ok = t < T && e < d;
-      const long long off = base + (long long)t * d + e;
+      const bool ok = t < Tk && e < d;
+      const long long off = kbase + (long long)t * d + e;
       Kt[e * kLDT + r] = ok ? load_elem(p.kh, off, p.hat_dtype) : 0.f;
       Vs[r * DA + e] = ok ? load_elem(p.vh, off, p.hat_dtype) : 0.f;
     }
@@ -113,12 +116,12 @@ __global__ void __launch_bounds__(kAttnThreads) attn_fwd_simt_kernel(AttnArgs p)
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const int qi = q0 + r0 + i;
+      const int qi = gq0 + r0 + i;
       float mx = -INFINITY;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int kj = k0 + c0 + j;
-        s[i][j] = (kj <= qi && kj < T) ? s[i][j] * p.scale : -INFINITY;
+        s[i][j] = (kj <= qi && kj < Tk) ? s[i][j] * p.scale : -INFINITY;
         mx = fmaxf(mx, s[i][j]);
       }
 #pragma unroll
@@ -159,9 +162,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_fwd_simt_kernel(AttnArgs p)
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int t = q0 + r0 + i;
-    if (t >= T) continue;
+    if (t >= Tq) continue;
     const float inv = 1.f / fmaxf(lrow[i], 1e-20f);
-    float* orow = p.o + ((long long)chain * T + t) * d;
+    float* orow = p.o + ((long long)chain * Tq + t) * d;
 #pragma unroll
     for (int j = 0; j < CPT; ++j) {
       const int e = tx * CPT + j;
@@ -176,7 +179,7 @@ int launch_attn(const AttnArgs& a, int BH, cudaStream_t s) {
   if (cudaFuncSetAttribute(attn_fwd_simt_kernel<DA>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)Cf::kSmem) != cudaSuccess)
     return HOA_ERR_LAUNCH;
-  dim3 grid((unsigned)ceil_div(a.T, kBQ), (unsigned)BH);
+  dim3 grid((unsigned)ceil_div(a.Tq, kBQ), (unsigned)BH);
   attn_fwd_simt_kernel<DA><<<grid, kAttnThreads, Cf::kSmem, s>>>(a);
   return launch_status();
 }
@@ -186,11 +189,13 @@ int launch_attn(const AttnArgs& a, int BH, cudaStream_t s) {
 using namespace hoa;
 
 extern "C" int hoa_attn_fwd(const void* qh, const void* kh, const void* vh, int hat_dtype,
-                            float* o, float softmax_scale, int BH, int T, int d, void* stream) {
-  if (!qh || !kh || !vh || !o || BH < 1 || T < 1 || d < 1) return HOA_ERR_INVALID_ARG;
+                            float* o, float softmax_scale, int BH, int Tq, int Tk, int q_offset,
+                            int d, void* stream) {
+  if (!qh || !kh || !vh || !o || BH < 1 || Tq < 1 || Tk < 1 || d < 1) return HOA_ERR_INVALID_ARG;
+  if (q_offset < 0 || q_offset + Tq > Tk) return HOA_ERR_INVALID_ARG;
   if (hat_dtype != HOA_F32 && hat_dtype != HOA_BF16) return HOA_ERR_UNSUPPORTED;
   if (BH > 65535) return HOA_ERR_UNSUPPORTED;
-  AttnArgs a{qh, kh, vh, hat_dtype, o, softmax_scale, T, d};
+  AttnArgs a{qh, kh, vh, hat_dtype, o, softmax_scale, Tq, Tk, q_offset, d};
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int da = ((d + 15) / 16) * 16;
   switch (da) {

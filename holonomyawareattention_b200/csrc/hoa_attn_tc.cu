@@ -11,7 +11,9 @@
 //   P   = exp2(S*scale*log2e - m) as bf16, written to shared memory (swizzled)
 //   O_j = P V        M=128, N=d (padded to 16),  K=128 keys -> TMEM columns [128, 128+d)
 //   o  <- o * exp2(m_old - m_new) + O_j  (fp32, per-row accumulator in shared memory)
-// Output: o / l in fp32, (B*H, T, d), consumed by the inverse transport (kernel 4).
+// Output: o / l in fp32, (B*H, Tq, d), consumed by the inverse transport (kernel 4).
+// Queries may be a shard of the sequence: local row i is global position
+// q_offset + i and attends to keys 0 .. q_offset + i of the (gathered) key set.
 #include <cudaTypedefs.h>
 
 #include "hoa_sm100.cuh"
@@ -40,7 +42,7 @@ struct TcLayout {
 struct AttnTcArgs {
   float* o;
   int* status;
-  int T, d;
+  int Tq, Tk, q_offset, d;   // query rows are global positions q_offset .. q_offset + Tq - 1
   float scale_log2;
 };
 
@@ -68,8 +70,10 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
   const int tid = threadIdx.x, warp = tid >> 5;
   const int chain = blockIdx.y;
   const int qt = gridDim.x - 1 - blockIdx.x;     // heaviest causal tiles first
-  const int q0 = qt * 128;
-  const int T = p.T, d = p.d;
+  const int q0 = qt * 128;                        // local query row of this tile
+  const int Tq = p.Tq, Tk = p.Tk, d = p.d;
+  const int gq0 = p.q_offset + q0;                // global position of its first row
+  const int nkt = min((gq0 + 127) / 128, (Tk - 1) / 128) + 1;   // key tiles this tile sees
 
   if (tid == 0) {
     mbar_init(bar_tma, 1);
@@ -104,12 +108,12 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
   bool bad = !mbar_wait(bar_tma, ph_tma);
   ph_tma ^= 1;
 
-  const int qi = q0 + tid;
+  const int qi = gq0 + tid;                        // this thread's global query position
   float m_run = -INFINITY, l_run = 0.f;
 #pragma unroll 8
   for (int e = 0; e < DP16; ++e) sO[e * 128 + tid] = 0.f;    // this row's accumulator
 
-  for (int j = 0; j <= qt; ++j) {
+  for (int j = 0; j < nkt; ++j) {
     if (__syncthreads_or(bad)) { bad = true; break; }
     const int k0 = j * 128;
     if (tid == 0) {
@@ -144,7 +148,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         const int key = k0 + c * 16 + i;
-        if (key <= qi && key < T) mt = fmaxf(mt, v[i]);
+        if (key <= qi && key < Tk) mt = fmaxf(mt, v[i]);
       }
     }
     const float m_new = fmaxf(m_run, mt * p.scale_log2);
@@ -159,9 +163,9 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
 #pragma unroll
       for (int i = 0; i < 16; i += 2) {
         const int key = k0 + c * 16 + i;
-        const float p0 = (key <= qi && key < T) ? exp2f(fmaf(v[i], p.scale_log2, -m_new)) : 0.f;
+        const float p0 = (key <= qi && key < Tk) ? exp2f(fmaf(v[i], p.scale_log2, -m_new)) : 0.f;
         const float p1 =
-            (key + 1 <= qi && key + 1 < T) ? exp2f(fmaf(v[i + 1], p.scale_log2, -m_new)) : 0.f;
+            (key + 1 <= qi && key + 1 < Tk) ? exp2f(fmaf(v[i + 1], p.scale_log2, -m_new)) : 0.f;
         rs += p0 + p1;
         pk[i >> 1] = pack_bf16x2(p0, p1);
       }
@@ -206,9 +210,9 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
   }
 
   bad = __syncthreads_or(bad);
-  if (qi < T && !bad) {
+  if (q0 + tid < Tq && !bad) {
     const float inv = 1.f / fmaxf(l_run, 1e-20f);
-    float* orow = p.o + ((long long)chain * T + qi) * d;
+    float* orow = p.o + ((long long)chain * Tq + q0 + tid) * d;
     for (int e = 0; e < d; ++e) orow[e] = sO[e * 128 + tid] * inv;
   }
   if (bad && tid == 0 && p.status != nullptr) atomicExch(p.status, HOA_ERR_TIMEOUT);
@@ -259,7 +263,7 @@ static int launch_tc(const CUtensorMap& mq, const CUtensorMap& mk, const CUtenso
   if (cudaFuncSetAttribute(attn_tc_kernel<DP16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            L::kAlloc) != cudaSuccess)
     return HOA_ERR_LAUNCH;
-  dim3 grid((unsigned)ceil_div(a.T, 128), (unsigned)BH);
+  dim3 grid((unsigned)ceil_div(a.Tq, 128), (unsigned)BH);
   attn_tc_kernel<DP16><<<grid, kTcThreads, L::kAlloc, s>>>(mq, mk, mv, a);
   return launch_status();
 }
@@ -273,18 +277,19 @@ using namespace hoa;
 extern "C" int hoa_vt_stride(int T) { return ((T + 7) / 8) * 8; }
 
 extern "C" int hoa_attn_tc_fwd(const void* qh, const void* kh, const void* vhT, float* o,
-                               int* status, float softmax_scale, int BH, int T, int d,
-                               void* stream) {
-  if (!qh || !kh || !vhT || !o || BH < 1 || T < 1 || d < 1) return HOA_ERR_INVALID_ARG;
+                               int* status, float softmax_scale, int BH, int Tq, int Tk,
+                               int q_offset, int d, void* stream) {
+  if (!qh || !kh || !vhT || !o || BH < 1 || Tq < 1 || Tk < 1 || d < 1) return HOA_ERR_INVALID_ARG;
+  if (q_offset < 0 || q_offset + Tq > Tk) return HOA_ERR_INVALID_ARG;
   if (BH > 65535 || d > 128 || d % 8 != 0) return HOA_ERR_UNSUPPORTED;
   const int dp16 = ((d + 15) / 16) * 16;
-  const uint64_t tp = (uint64_t)hoa_vt_stride(T);
+  const uint64_t tp = (uint64_t)hoa_vt_stride(Tk);
   CUtensorMap mq, mk, mv;
-  if (!make_map(&mq, qh, d, T, BH, (uint64_t)d * 2, (uint64_t)T * d * 2, 128) ||
-      !make_map(&mk, kh, d, T, BH, (uint64_t)d * 2, (uint64_t)T * d * 2, 128) ||
-      !make_map(&mv, vhT, T, d, BH, tp * 2, tp * d * 2, (uint32_t)d))
+  if (!make_map(&mq, qh, d, Tq, BH, (uint64_t)d * 2, (uint64_t)Tq * d * 2, 128) ||
+      !make_map(&mk, kh, d, Tk, BH, (uint64_t)d * 2, (uint64_t)Tk * d * 2, 128) ||
+      !make_map(&mv, vhT, Tk, d, BH, tp * 2, tp * d * 2, (uint32_t)d))
     return HOA_ERR_INVALID_ARG;
-  AttnTcArgs a{o, status, T, d, softmax_scale * 1.4426950408889634f};
+  AttnTcArgs a{o, status, Tq, Tk, q_offset, d, softmax_scale * 1.4426950408889634f};
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   switch (dp16) {
     case 16: return launch_tc<16>(mq, mk, mv, a, BH, s);

@@ -688,8 +688,8 @@ extern "C" int hoa_core_forward(const void* a_all, int a_dtype, const float* a_b
   if (st != HOA_OK) return st;
   st = hoa_carry_apply(U, C, qh, kh, vh, hat_dtype, L.vt_stride, B * H, T, d, chunk, stream);
   if (st != HOA_OK) return st;
-  st = L.tc ? hoa_attn_tc_fwd(qh, kh, vh, o, status, softmax_scale, B * H, T, d, stream)
-            : hoa_attn_fwd(qh, kh, vh, hat_dtype, o, softmax_scale, B * H, T, d, stream);
+  st = L.tc ? hoa_attn_tc_fwd(qh, kh, vh, o, status, softmax_scale, B * H, T, T, 0, d, stream)
+            : hoa_attn_fwd(qh, kh, vh, hat_dtype, o, softmax_scale, B * H, T, T, 0, d, stream);
   if (st != HOA_OK) return st;
   return hoa_out_transport(o, R, C, chunk, out, out_dtype, B, H, T, d, stream);
 }

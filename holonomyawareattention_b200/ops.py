@@ -158,26 +158,35 @@ def carry_apply(U: torch.Tensor, C: torch.Tensor, chunk: int, hat_dtype: torch.d
 
 
 def attn_fwd(qh: torch.Tensor, kh: torch.Tensor, vh: torch.Tensor,
-             softmax_scale: float) -> torch.Tensor:
-    """Kernel (3), fp32 SIMT path: o = softmax(q^ k^T * scale, causal) v^ -> (BH,T,d) fp32."""
+             softmax_scale: float, q_offset: int = 0) -> torch.Tensor:
+    """Kernel (3), fp32 SIMT path: o = softmax(q^ k^T * scale, causal) v^ -> (BH,Tq,d) fp32.
+
+    q^ (BH,Tq,d) holds global positions q_offset.., k^/v^ (BH,Tk,d) positions 0..Tk-1."""
     _need_cuda(qh, kh, vh)
-    BH, T, d = qh.shape
-    o = torch.empty(BH, T, d, dtype=torch.float32, device=qh.device)
+    BH, Tq, d = qh.shape
+    Tk = kh.shape[1]
+    o = torch.empty(BH, Tq, d, dtype=torch.float32, device=qh.device)
     _lib.call("hoa_attn_fwd", _ptr(qh), _ptr(kh), _ptr(vh), _dtype_code(qh.dtype), _ptr(o),
-              float(softmax_scale), BH, T, d, _stream(qh.device))
+              float(softmax_scale), BH, Tq, Tk, int(q_offset), d, _stream(qh.device))
     return o
 
 
 def attn_tc_fwd(qh: torch.Tensor, kh: torch.Tensor, vhT: torch.Tensor, softmax_scale: float,
-                status: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """Kernel (3), tcgen05 bf16 path (v^ transposed) -> o (BH,T,d) fp32."""
+                status: Optional[torch.Tensor] = None, q_offset: int = 0) -> torch.Tensor:
+    """Kernel (3), tcgen05 bf16 path (v^ transposed) -> o (BH,Tq,d) fp32.
+
+    q^ (BH,Tq,d) holds global positions q_offset.., k^ (BH,Tk,d) and
+    v^T (BH,d,vt_stride(Tk)) positions 0..Tk-1."""
     _need_cuda(qh, kh, vhT)
-    BH, T, d = qh.shape
+    BH, Tq, d = qh.shape
+    Tk = kh.shape[1]
     if qh.dtype != torch.bfloat16:
         raise NotImplementedError("the tensor-core attention takes bf16 q^/k^/v^")
-    o = torch.empty(BH, T, d, dtype=torch.float32, device=qh.device)
+    if vhT.shape != (BH, d, vt_stride(Tk)):
+        raise ValueError(f"v^T must be (BH, d, vt_stride(Tk)) = ({BH}, {d}, {vt_stride(Tk)})")
+    o = torch.empty(BH, Tq, d, dtype=torch.float32, device=qh.device)
     _lib.call("hoa_attn_tc_fwd", _ptr(qh), _ptr(kh), _ptr(vhT), _ptr(o), _ptr(status),
-              float(softmax_scale), BH, T, d, _stream(qh.device))
+              float(softmax_scale), BH, Tq, Tk, int(q_offset), d, _stream(qh.device))
     return o
 
 

@@ -122,23 +122,29 @@ int hoa_carry_apply(const float* U, const float* C, void* qh, void* kh, void* vh
 int hoa_vt_stride(int T);
 
 /*
- * Kernel (3), fp32 path: causal online-softmax attention on q^/k^/v^
- * (B*H, T, d) in fp32 (or bf16) with every product in fp32; writes the
- * normalised o = softmax(q^ k^T * scale) v^ as (B*H, T, d) fp32.
+ * Kernel (3), fp32 path: causal online-softmax attention with every product
+ * in fp32.  q^ is (B*H, Tq, d), k^ and v^ (B*H, Tk, d), in fp32 (or bf16).
+ * Query row i is global position q_offset + i and attends to keys
+ * 0 .. q_offset + i (q_offset + Tq <= Tk; a whole sequence is Tq = Tk,
+ * q_offset = 0; a sequence shard passes its offset and the gathered keys).
+ * Writes the normalised o = softmax(q^ k^T * scale) v^ as (B*H, Tq, d) fp32.
  * Replaces core/attention_fast_chunked.py:119-168 (kernel/attention_kernel.py:122-134
  * run_fwd_kernel) for the causal tril mask.
  */
 int hoa_attn_fwd(const void* qh, const void* kh, const void* vh, int hat_dtype,
-                 float* o, float softmax_scale, int BH, int T, int d, void* stream);
+                 float* o, float softmax_scale, int BH, int Tq, int Tk, int q_offset,
+                 int d, void* stream);
 
 /*
  * Kernel (3), bf16 path on tcgen05/TMEM: same contract as hoa_attn_fwd with
- * bf16 q^, k^ (B*H, T, d) and v^ transposed (B*H, d, hoa_vt_stride(T));
- * fp32 accumulation.  d % 8 == 0, d <= 128.  `status` (nullable device int)
- * receives HOA_ERR_TIMEOUT if a bounded wait gave up.
+ * bf16 q^ (B*H, Tq, d), k^ (B*H, Tk, d) and v^ transposed
+ * (B*H, d, hoa_vt_stride(Tk)); fp32 accumulation.  d % 8 == 0, d <= 128.
+ * `status` (nullable device int) receives HOA_ERR_TIMEOUT if a bounded wait
+ * gave up.
  */
 int hoa_attn_tc_fwd(const void* qh, const void* kh, const void* vhT, float* o, int* status,
-                    float softmax_scale, int BH, int T, int d, void* stream);
+                    float softmax_scale, int BH, int Tq, int Tk, int q_offset, int d,
+                    void* stream);
 
 /*
  * Kernel (4): inverse transport out_t = R_t (C_{t/chunk} o_t), written to

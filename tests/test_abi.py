@@ -61,8 +61,8 @@ def test_invalid_arguments_rejected_without_gpu(lib):
     null = None
     # null pointers -> HOA_ERR_INVALID_ARG (1) before any CUDA call
     assert lib.hoa_link_local(null, 0, null, 1.0, null, 0, null, null, null, 1, 1, 4, 8, 4, null) == 1
-    assert lib.hoa_attn_fwd(null, null, null, 0, null, 1.0, 1, 4, 8, null) == 1
-    assert lib.hoa_attn_tc_fwd(null, null, null, null, null, 1.0, 1, 4, 8, null) == 1
+    assert lib.hoa_attn_fwd(null, null, null, 0, null, 1.0, 1, 4, 4, 0, 8, null) == 1
+    assert lib.hoa_attn_tc_fwd(null, null, null, null, null, 1.0, 1, 4, 4, 0, 8, null) == 1
     assert lib.hoa_out_transport(null, null, null, 4, null, 0, 1, 1, 4, 8, null) == 1
     assert lib.hoa_carry_scan(null, null, null, null, 1, 1, 8, null) == 1
     # unsupported head dim -> HOA_ERR_UNSUPPORTED (2)
@@ -71,8 +71,10 @@ def test_invalid_arguments_rejected_without_gpu(lib):
     # bad dtype code
     assert lib.hoa_link_local(dummy, 7, null, 1.0, dummy, 0, dummy, dummy, dummy, 1, 1, 4, 8, 4, null) == 2
     # tensor-core attention needs d % 8 == 0 and d <= 128
-    assert lib.hoa_attn_tc_fwd(dummy, dummy, dummy, dummy, null, 1.0, 1, 4, 12, null) == 2
-    assert lib.hoa_attn_tc_fwd(dummy, dummy, dummy, dummy, null, 1.0, 1, 4, 136, null) == 2
+    assert lib.hoa_attn_tc_fwd(dummy, dummy, dummy, dummy, null, 1.0, 1, 4, 4, 0, 12, null) == 2
+    assert lib.hoa_attn_tc_fwd(dummy, dummy, dummy, dummy, null, 1.0, 1, 4, 4, 0, 136, null) == 2
+    # a query shard must lie inside the key range
+    assert lib.hoa_attn_tc_fwd(dummy, dummy, dummy, dummy, null, 1.0, 1, 4, 8, 6, 16, null) == 1
     assert lib.hoa_vt_stride(4093) == 4096 and lib.hoa_vt_stride(8) == 8
     # workspace too small -> HOA_ERR_WORKSPACE (4)
     assert lib.hoa_core_forward(dummy, 0, null, 1.0, dummy, 0, dummy, 0, 0, 1.0, null, null,
