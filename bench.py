@@ -202,6 +202,16 @@ def config_obj(name, n):
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
+def generator_precision_label(mod, T, dtype):
+    """The edge-MLP precision the timed forward used ("fp32" for a float32
+    module; T None: a sequence shard)."""
+    import torch
+    if dtype == torch.float32:
+        return "fp32"
+    eff = "split" if mod._split_generators(T) else "bf16"
+    return f"{eff} (auto)" if mod.generator_precision == "auto" else eff
+
+
 def run_ours(args):
     import numpy as np
     import torch
@@ -369,7 +379,7 @@ def run_ours(args):
         "e2e": {"value": world * B * T / (e2e_ms / 1e3), "unit": "tokens/s",
                 "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes},
         "gpu_launches": 5 * args.steps, "clocks": clk,
-        "generator_precision": mod.generator_precision,
+        "generator_precision": generator_precision_label(mod, T, dtype),
         **extra,
     }
     if rank == 0:
@@ -486,7 +496,7 @@ def run_seq_sharded(args):
                 "h2d_bytes_per_step": xs.numel() * xs.element_size(),
                 "d2h_bytes_per_step": xs.numel() * xs.element_size()},
         "gpu_launches": 6 * args.steps, "clocks": clk,
-        "generator_precision": mod.generator_precision,
+        "generator_precision": generator_precision_label(mod, T, dtype),
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
@@ -501,7 +511,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--config", default="c3", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--generator-precision", default=None, choices=[None, "split", "bf16"])
+    ap.add_argument("--generator-precision", default=None, choices=[None, "auto", "split", "bf16"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--traffic", type=float, default=None,
                     help="ncu dram bytes per link_local launch, from a capture (scaled), if known")

@@ -57,8 +57,9 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
                const __grid_constant__ CUtensorMap tv, AttnTcArgs p) {
   using L = TcLayout<DP16>;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                           ~static_cast<uintptr_t>(1023));
+  // 1024-aligned base by pointer arithmetic on the shared array, so that the
+  // compiler keeps every derived pointer in the shared address space
+  uint8_t* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t* sQ = sm + L::offQ;
   uint8_t* sK = sm + L::offK;
   uint8_t* sV = sm + L::offV;

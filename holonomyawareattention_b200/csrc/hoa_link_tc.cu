@@ -42,11 +42,16 @@ constexpr float kTheta8tc = 0.6f;
 
 template <int DP>
 struct LtLayout {
-  // Thread layout: 4 TMEM lane groups (warps w % 4) x CQ column groups (warps w / 4).
-  static constexpr int CQ = (DP % 32 == 0) ? 4 : 2;
+  // Compute threads: 4 TMEM lane groups (warps w % 4) x CQ column groups
+  // (warps w / 4); one more warp issues the tensor-core products.
+  // (d = 96 uses 3 column groups: with 13 warps every SM sub-partition holds
+  // at most 4, which leaves 128 registers per thread.)
+  static constexpr int CQ = (DP == 96) ? 3 : ((DP % 32 == 0) ? 4 : 2);
   static constexpr int CW = DP / CQ;                   // columns per thread
   static constexpr int NCH = CW / 8;                   // 8-column chunks per thread
-  static constexpr int NT = 128 * CQ;
+  static constexpr int NT = 128 * CQ;                  // compute threads
+  static constexpr int NW = NT / 32;                   // compute warps
+  static constexpr int NTHREADS = NT + 32;             // + the MMA warp
   static_assert(CW % 8 == 0, "column groups must be multiples of 8");
   static constexpr int NSLAB = (DP + 31) / 32;
   static constexpr int kSlab = DP * 128;               // DP rows of 128 bytes
@@ -57,20 +62,20 @@ struct LtLayout {
   static constexpr int offYlo = kMat;
   static constexpr int offXhi = 2 * kMat;
   static constexpr int offXlo = 3 * kMat;
-  static constexpr int offXT = 4 * kMat;               // fp32 scratch: [DP][DP+1] transpose, or reductions
-  static constexpr int kXTmat = DP * (DP + 1) * 4;
-  static constexpr int kXTred = CQ * 3 * 128 * 4;
-  static constexpr int kXTbytes = kXTmat > kXTred ? kXTmat : kXTred;
+  static constexpr int offXT = 4 * kMat;               // fp32 [DP][DP+1] transpose scratch
+  static constexpr int kXTbytes = DP * (DP + 1) * 4;
   static constexpr int kXend = offXlo + (NSLAB - 1) * kSlab + 128 * 128;
   static constexpr int kEnd0 = offXT + kXTbytes > kXend ? offXT + kXTbytes : kXend;
   static constexpr int offStage = (kEnd0 + 1023) / 1024 * 1024;
   // one stage: the generator a_t (fp32) followed by q, k, v of position t (up to fp32)
   static constexpr int kGenBytes = (DP * (DP - 1) / 2) * 4;
   static constexpr int kStage = (kGenBytes + 3 * DP * 4 + 127) / 128 * 128;
-  static constexpr int offRed = offStage + 2 * kStage;
-  static constexpr int offBar = offRed + 64;
-  static constexpr int kBytes = offBar + 64;
-  // TMEM: R^T hi, R^T lo, A, D1, D2 (DP columns each), rounded up to a power of two.
+  static constexpr int offU = offStage + 2 * kStage;   // U partial sums [CQ][3][128]
+  static constexpr int offMisc = offU + CQ * 3 * 128 * 4;
+  static constexpr int offBar = offMisc + 64;
+  static constexpr int kBytes = offBar + 128;
+  static_assert(NCH <= 4, "one operand barrier per column chunk, at most 4");
+  // TMEM: R^T hi, R^T lo, A, P, Q (DP columns each), rounded up to a power of two.
   static constexpr uint32_t kTmemCols = 5 * DP <= 128 ? 128 : (5 * DP <= 256 ? 256 : 512);
   // Request enough shared memory that no more CTAs share an SM than its 512
   // TMEM columns can serve (an allocation would otherwise wait for a peer).
@@ -83,26 +88,11 @@ struct LtLayout {
 
 struct LinkTcArgs {
   const float* a; const float* a_bias; float edge_scale;
-  const void* qkv; int qkv_dtype;
+  const void* qkv;
   float* R; float* U; float* M;
   int* status;
   int B, H, T, chunk, K;
 };
-
-// Row r, columns [c0, c0+8) of A = skew(edge_scale * a) from the staged vector.
-// S_i = i (2d - i - 1) / 2 is the offset of row i's strict upper triangle.
-template <int DP>
-HOA_DEVICE void skew_row8(const float* __restrict__ av, float es, int r, int c0, float (&v)[8]) {
-  const int Sr = r * (2 * DP - r - 1) / 2;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int c = c0 + i;
-    float x = 0.f;
-    if (c > r) x = __fmul_rn(av[Sr + c - r - 1], es);
-    else if (c < r) x = -__fmul_rn(av[c * (2 * DP - c - 1) / 2 + r - c - 1], es);
-    v[i] = x;
-  }
-}
 
 // Write 8 values of row `row`, columns [c0, c0+8), as tf32 hi (rounded) and
 // lo = x - hi (exact; the tensor core reads its leading tf32 bits) into two
@@ -126,87 +116,133 @@ HOA_DEVICE void put_row8(uint8_t* hi_buf, uint8_t* lo_buf, int row, int c0, cons
   }
 }
 
-// 3-pass SS product D = X Y with X given as rows and Y as the rows of Y^T
-// (both K-major, 128B-swizzled).
+// One 8-column chunk j of every column group (K-steps q * NCH + j) of a 3-pass
+// SS product D = X Y, X given as rows and Y as the rows of Y^T (both K-major,
+// 128B-swizzled).  Chunk 0 (q = 0, first pass) starts the accumulation.
 template <int DP>
-HOA_DEVICE void issue_ss(uint32_t d_tmem, uint32_t xhi, uint32_t xlo, uint32_t yhi, uint32_t ylo) {
+HOA_DEVICE void issue_ss_chunk(uint32_t d_tmem, uint32_t xhi, uint32_t xlo, uint32_t yhi, uint32_t ylo,
+                               int j) {
   using L = LtLayout<DP>;
   constexpr uint32_t id = make_idesc(kFmtTF32, 128, DP);
   const uint32_t xs[3] = {xhi, xhi, xlo};
   const uint32_t ys[3] = {yhi, ylo, yhi};
 #pragma unroll
-  for (int ps = 0; ps < 3; ++ps)
+  for (int q = 0; q < L::CQ; ++q) {
+    const int kk = q * L::NCH + j;
+    const uint32_t off = (kk >> 2) * L::kSlab + (kk & 3) * 32;
 #pragma unroll
-    for (int kk = 0; kk < DP / 8; ++kk) {
-      const uint32_t off = (kk >> 2) * L::kSlab + (kk & 3) * 32;
-      mma_tf32(d_tmem, desc_sw128(xs[ps] + off), desc_sw128(ys[ps] + off), id, (ps | kk) ? 1u : 0u);
-    }
+    for (int ps = 0; ps < 3; ++ps)
+      mma_tf32(d_tmem, desc_sw128(xs[ps] + off), desc_sw128(ys[ps] + off), id, (j | q | ps) ? 1u : 0u);
+  }
 }
 
-// 3-pass TS product D = A B^T: A from TMEM (hi, lo columns), B rows K-major in shared memory.
+// The same for a 3-pass TS product D = A B^T: A from TMEM (hi, lo columns),
+// B rows K-major in shared memory.
 template <int DP>
-HOA_DEVICE void issue_ts(uint32_t d_tmem, uint32_t ahi, uint32_t alo, uint32_t bhi, uint32_t blo) {
+HOA_DEVICE void issue_ts_chunk(uint32_t d_tmem, uint32_t ahi, uint32_t alo, uint32_t bhi, uint32_t blo,
+                               int j) {
   using L = LtLayout<DP>;
   constexpr uint32_t id = make_idesc(kFmtTF32, 128, DP);
   const uint32_t as[3] = {ahi, ahi, alo};
   const uint32_t bs[3] = {bhi, blo, bhi};
 #pragma unroll
-  for (int ps = 0; ps < 3; ++ps)
+  for (int q = 0; q < L::CQ; ++q) {
+    const int kk = q * L::NCH + j;
+    const uint32_t off = (kk >> 2) * L::kSlab + (kk & 3) * 32;
 #pragma unroll
-    for (int kk = 0; kk < DP / 8; ++kk) {
-      const uint32_t ba = bs[ps] + (kk >> 2) * L::kSlab + (kk & 3) * 32;
-      mma_tf32_ts(d_tmem, as[ps] + kk * 8, desc_sw128(ba), id, (ps | kk) ? 1u : 0u);
-    }
+    for (int ps = 0; ps < 3; ++ps)
+      mma_tf32_ts(d_tmem, as[ps] + kk * 8, desc_sw128(bs[ps] + off), id, (j | q | ps) ? 1u : 0u);
+  }
 }
 
-// Barrier for operand hand-over: generic shared-memory writes become visible
-// to the tensor core, TMEM accesses are ordered around the barrier.
-HOA_DEVICE void operand_barrier() {
+// Hand-over of operands from the compute warps to the MMA warp: each thread
+// makes its generic shared-memory writes visible to the tensor core's proxy
+// and orders its TMEM accesses; the warp converges and one lane arrives (the
+// barrier counts one arrival per compute warp).
+HOA_DEVICE void hand_over(uint64_t* bar, int lid) {
   fence_proxy_async_smem();
   tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
+  __syncwarp();
+  if (lid == 0) mbar_arrive(bar);
 }
 
-template <int DP>
-__global__ void __launch_bounds__(LtLayout<DP>::NT, 1) link_tc_kernel(LinkTcArgs p) {
+// Loads of the per-position vectors q, k, v (8 consecutive elements from
+// shared memory: one 16-byte load for bf16, two for fp32).
+template <bool QB16>
+HOA_DEVICE void load8(const uint8_t* base, int i0, float (&v)[8]) {
+  if constexpr (QB16) {
+    const uint4 w = *reinterpret_cast<const uint4*>(base + 2 * i0);
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      v[2 * i] = __uint_as_float(ws[i] << 16);
+      v[2 * i + 1] = __uint_as_float(ws[i] & 0xffff0000u);
+    }
+  } else {
+    const float4 a = *reinterpret_cast<const float4*>(base + 4 * i0);
+    const float4 b = *reinterpret_cast<const float4*>(base + 4 * i0 + 16);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  }
+}
+
+// Warp roles.  Compute warps 0 .. NW-1 own the rows (TMEM lanes) and do all
+// elementwise work; warp NW (one elected lane) only issues the products.
+// Each product's operands are handed over through an mbarrier (one arrival per
+// compute warp) and its completion is signalled by tcgen05.commit, so the
+// issuing thread never stalls the elementwise work.  Per position t, with
+// fixed TMEM roles (cA: A, then N0; cQ: every expm product; cP: the
+// composition), the tensor-core order is P2(t), P3(t) [, squarings], P4(t),
+// P1(t+1), and the compute warps overlap
+//   build A(t+1)                    with P4(t),
+//   R_{t+1} = R_t + P4 into TMEM    with P1(t+1),
+//   R_{t+1}, U_{t+1} to global      with P2(t+1).
+template <int DP, bool QB16>
+__global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, 1) link_tc_kernel(LinkTcArgs p) {
   using L = LtLayout<DP>;
-  constexpr int NCH = L::NCH, CW = L::CW, CQ = L::CQ, NT = L::NT;
+  constexpr int NCH = L::NCH, CW = L::CW, CQ = L::CQ, NT = L::NT, NW = L::NW;
   constexpr int m = DP * (DP - 1) / 2;
+  constexpr int kQkvBytes = 3 * DP * (QB16 ? 2 : 4);
+  constexpr uint32_t kNamed = 1;                          // named barrier of the compute warps
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                           ~static_cast<uintptr_t>(1023));
+  // 1024-aligned base by pointer arithmetic on the shared array, so that the
+  // compiler keeps every derived pointer in the shared address space
+  uint8_t* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t* Yhi = sm + L::offYhi;
   uint8_t* Ylo = sm + L::offYlo;
   uint8_t* Xhi = sm + L::offXhi;
   uint8_t* Xlo = sm + L::offXlo;
   float* XT = reinterpret_cast<float*>(sm + L::offXT);
   uint8_t* stage_base = sm + L::offStage;
-  float* sred = reinterpret_cast<float*>(sm + L::offRed);
-  uint64_t* bar_mma = reinterpret_cast<uint64_t*>(sm + L::offBar);  // P2, P3, squarings, P4
-  uint64_t* bar_p1 = bar_mma + 1;                                    // P1
-  uint64_t* bar_a = bar_mma + 2;                                     // two: one per stage
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_a + 2);
+  float* sU = reinterpret_cast<float*>(sm + L::offU);
+  int* smax = reinterpret_cast<int*>(sm + L::offMisc);           // [2][4] theta^2 partial maxima
+  int* s_nsq = smax + 8;                                           // squarings of this position
+  volatile int* s_abort = smax + 9;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::offBar);
+  // operands ready (compute -> MMA), one barrier per column chunk j: P1 has its
+  // own set (its hand-over follows P4's without a wait in between); P2, P3,
+  // squarings and P4 share the other
+  uint64_t* ops_main = bars + 0;   // [NCH]
+  uint64_t* ops_p1 = bars + 4;     // [NCH]
+  uint64_t* done_p1 = bars + 8;    // product complete (MMA -> compute)
+  uint64_t* done_mma = bars + 9;   // P2, P3, squarings
+  uint64_t* done_p4 = bars + 10;
+  uint64_t* done_fin = bars + 11;
+  uint64_t* bar_a = bars + 12;     // two: one per stage
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
 
   const int tid = threadIdx.x, warp = tid >> 5, lid = tid & 31;
-  const int g = warp & 3, q = warp >> 2;
-  const int r = g * 32 + lid;                            // this thread's row
-  const int c0 = q * CW;                                 // ... and its first column
-  const bool row_ok = r < DP;
   const int chain = blockIdx.x / p.K;
   const int kc = blockIdx.x % p.K;
   const int b = chain / p.H, h = chain % p.H;
   const int t0 = kc * p.chunk;
   const int t1 = min(t0 + p.chunk, p.T);
-  const float es = p.edge_scale;
-  const int qkv_bytes = 3 * DP * (p.qkv_dtype == HOA_BF16 ? 2 : 4);
-  const uint32_t stage_tx = (uint32_t)(L::kGenBytes + qkv_bytes);
 
   if (tid == 0) {
-    mbar_init(bar_mma, 1);
-    mbar_init(bar_p1, 1);
-    mbar_init(&bar_a[0], 1);
-    mbar_init(&bar_a[1], 1);
+    for (int i = 0; i < 14; ++i) mbar_init(&bars[i], (i < 8) ? NW : 1);
+    for (int i = 0; i < 8; ++i) smax[i] = 0;
+    *s_nsq = 0;
+    *s_abort = 0;
     fence_mbar_init();
   }
   if (warp == 0) {
@@ -217,374 +253,428 @@ __global__ void __launch_bounds__(LtLayout<DP>::NT, 1) link_tc_kernel(LinkTcArgs
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
-  const uint32_t lane = static_cast<uint32_t>(g * 32) << 16;
-  const uint32_t cRhi = tbase, cRlo = tbase + DP, cA = tbase + 2 * DP, cD1 = tbase + 3 * DP,
-                 cD2 = tbase + 4 * DP;
+  const uint32_t cRhi = tbase, cRlo = tbase + DP, cA = tbase + 2 * DP, cP = tbase + 3 * DP,
+                 cQ = tbase + 4 * DP;
   const uint32_t sXhi = smem_u32(Xhi), sXlo = smem_u32(Xlo), sYhi = smem_u32(Yhi),
                  sYlo = smem_u32(Ylo);
-
-  auto stage_gen = [&](int s) { return reinterpret_cast<float*>(stage_base + s * L::kStage); };
-  auto stage_qkv = [&](int s) { return stage_base + s * L::kStage + L::kGenBytes; };
-  auto fetch = [&](int s, int t) {        // thread 0: a_t and (q, k, v)_t into stage s
-    const long long row = ((long long)b * p.T + t) * p.H + h;
-    mbar_arrive_expect_tx(&bar_a[s], stage_tx);
-    bulk_load(stage_gen(s), p.a + row * m, L::kGenBytes, &bar_a[s]);
-    bulk_load(stage_qkv(s),
-              static_cast<const uint8_t*>(p.qkv) + row * (long long)qkv_bytes, qkv_bytes, &bar_a[s]);
-  };
-  // the generator bias of this chain's head, held in registers (a few per thread)
-  constexpr int kBiasPer = (m + NT - 1) / NT;
-  float breg[kBiasPer];
-#pragma unroll
-  for (int k = 0; k < kBiasPer; ++k) {
-    const int i = tid + k * NT;
-    breg[k] = (p.a_bias != nullptr && i < m) ? p.a_bias[(long long)h * m + i] : 0.f;
-  }
-  auto add_bias = [&](int s) {            // all threads; a barrier must follow
-    if (p.a_bias == nullptr) return;
-    float* av = stage_gen(s);
-#pragma unroll
-    for (int k = 0; k < kBiasPer; ++k) {
-      const int i = tid + k * NT;
-      if (i < m) av[i] += breg[k];
-    }
-  };
-  // A rows (this thread's columns) from stage s -> TMEM (fp32) and X (tf32 hi, lo)
-  auto build_a = [&](int s) {
-    const float* av = stage_gen(s);
-#pragma unroll
-    for (int j = 0; j < NCH; ++j) {
-      float v[8];
-      if (row_ok) skew_row8<DP>(av, es, r, c0 + 8 * j, v);
-      else {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = 0.f;
-      }
-      tmem_st8(cA + lane + c0 + 8 * j, v);
-      if (row_ok) put_row8<DP>(Xhi, Xlo, r, c0 + 8 * j, v);
-    }
-    tmem_wait_st();
-  };
-
   bool bad = false;
-  uint32_t ph_mma = 0, ph_p1 = 0, ph_a0 = 0, ph_a1 = 0;
-  auto wait_stage = [&](int s) {
-    if (s == 0) { bad |= !mbar_wait(&bar_a[0], ph_a0); ph_a0 ^= 1; }
-    else { bad |= !mbar_wait(&bar_a[1], ph_a1); ph_a1 ^= 1; }
-  };
 
-  // ---- prologue: position t0 (R = I, U = (q, k, v)), A(t0), and P1(t0) -> D2
-  if (tid == 0) fetch(0, t0);
-  wait_stage(0);
-  add_bias(0);
-  __syncthreads();
-  {
-    const long long pos = (long long)chain * p.T + t0;
-    float* Rg = p.R + pos * DP * DP;
-    for (int i = tid; i < DP * DP; i += NT) Rg[i] = (i / DP == i % DP) ? 1.f : 0.f;
-    float* Ug = p.U + pos * 3 * DP;
-    const uint8_t* qv = stage_qkv(0);
-    for (int i = tid; i < 3 * DP; i += NT) Ug[i] = load_elem(qv, i, p.qkv_dtype);
-#pragma unroll
-    for (int j = 0; j < NCH; ++j) {
-      float v[8], z[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) { v[i] = (c0 + 8 * j + i == r) ? 1.f : 0.f; z[i] = 0.f; }
-      tmem_st8(cRhi + lane + c0 + 8 * j, v);
-      tmem_st8(cRlo + lane + c0 + 8 * j, z);
-    }
-  }
-  build_a(0);
-  operand_barrier();
-  if (tid == 0 && !bad) {
-    issue_ss<DP>(cD2, sXhi, sXlo, sXhi, sXlo);      // D = A A^T = -A^2
-    tc_commit(bar_p1);
-  }
-
-  const float x1 = kT8tc[0], x2 = kT8tc[1], x3 = kT8tc[2], x4 = kT8tc[3], x5 = kT8tc[4],
-              x6 = kT8tc[5], x7 = kT8tc[6], y2 = kT8tc[7];
-
-  for (int t = t0; t < t1; ++t) {
-    const int it = t - t0;
-    const int sidx = it & 1;
-    // TMEM roles alternate: P holds P1(t) = -A^2, Q the other accumulator
-    const uint32_t cP = sidx ? cD1 : cD2, cQ = sidx ? cD2 : cD1;
-    const bool last = (t + 1 == t1);
-    if (__syncthreads_or(bad)) { bad = true; break; }
-    if (tid == 0 && !last) {                 // stage sidx^1 was last read two positions ago
-      fence_proxy_async_smem();
-      fetch(sidx ^ 1, t + 1);
-    }
-
-    // ---- theta^2 = ||A^2||_1 (A^2 symmetric: max row abs-sum) ---------------
-    bad |= !mbar_wait(bar_p1, ph_p1);
-    ph_p1 ^= 1;
-    tc_fence_after();
-    {
-      float v[NCH][8];
-#pragma unroll
-      for (int j = 0; j < NCH; ++j) tmem_ld8(cP + lane + c0 + 8 * j, v[j]);
-      tmem_wait_ld();
-      float rs = 0.f;
-#pragma unroll
-      for (int j = 0; j < NCH; ++j)
-#pragma unroll
-        for (int i = 0; i < 8; ++i) rs += fabsf(v[j][i]);
-      XT[q * 128 + r] = row_ok ? rs : 0.f;
-      __syncthreads();
-      if (q == 0) {
-        float full = 0.f;
-#pragma unroll
-        for (int qq = 0; qq < CQ; ++qq) full += XT[qq * 128 + r];
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) full = fmaxf(full, __shfl_xor_sync(0xffffffffu, full, o));
-        if (lid == 0) sred[g] = full;
+  if (warp == NW) {
+    // ------------------------------------------------------------ MMA warp
+    if (lid == 0) {
+      uint32_t ph_main = 0, ph_p1 = 0;   // bit j: phase parity of barrier j of the set
+      // waits for chunk j of the set, then issues that chunk of the product
+      auto wait_chunk = [&](uint64_t* set, uint32_t& ph, int j) {
+        const bool ok = mbar_wait_abortable(&set[j], (ph >> j) & 1u, s_abort);
+        ph ^= 1u << j;
+        if (ok) tc_fence_after();
+        return ok;
+      };
+      auto product_ss = [&](uint64_t* set, uint32_t& ph, uint32_t d, uint32_t xh, uint32_t xl,
+                            uint32_t yh, uint32_t yl) {
+        for (int j = 0; j < NCH; ++j) {
+          if (!wait_chunk(set, ph, j)) return false;
+          issue_ss_chunk<DP>(d, xh, xl, yh, yl, j);
+        }
+        return true;
+      };
+      bool ok = product_ss(ops_p1, ph_p1, cQ, sXhi, sXlo, sXhi, sXlo);     // Q = A A^T = -A^2
+      if (ok) tc_commit(done_p1);
+      for (int t = t0; t < t1 && ok; ++t) {
+        // P2 (Q = A2s T1); the squaring count is published before chunk 0's hand-over
+        if (!wait_chunk(ops_main, ph_main, 0)) break;
+        const int nsq = *s_nsq;
+        issue_ss_chunk<DP>(cQ, sXhi, sXlo, sYhi, sYlo, 0);
+        for (int j = 1; j < NCH && ok; ++j) {
+          ok = wait_chunk(ops_main, ph_main, j);
+          if (ok) issue_ss_chunk<DP>(cQ, sXhi, sXlo, sYhi, sYlo, j);
+        }
+        if (!ok) break;
+        tc_commit(done_mma);
+        for (int sq = -1; sq < nsq && ok; ++sq) {                        // Q = L F, then Q = N N
+          ok = product_ss(ops_main, ph_main, cQ, sXhi, sXlo, sYhi, sYlo);
+          if (ok) tc_commit(done_mma);
+        }
+        for (int j = 0; j < NCH && ok; ++j) {                            // P = R^T N^T
+          ok = wait_chunk(ops_main, ph_main, j);
+          if (ok) issue_ts_chunk<DP>(cP, cRhi, cRlo, sYhi, sYlo, j);
+        }
+        if (!ok) break;
+        tc_commit(done_p4);
+        if (t + 1 < t1) {
+          ok = product_ss(ops_p1, ph_p1, cQ, sXhi, sXlo, sXhi, sXlo);
+          if (ok) tc_commit(done_p1);
+        }
       }
-      __syncthreads();
+      // every product issued above has completed before TMEM is released
+      tc_commit(done_fin);
+      bad |= !mbar_wait(done_fin, 0);
     }
-    int nsq = 0;
-    {
-      float theta = sqrtf(fmaxf(fmaxf(sred[0], sred[1]), fmaxf(sred[2], sred[3])));
-      while (theta > kTheta8tc && nsq < 64) { theta *= 0.5f; ++nsq; }
-    }
-    const float sa = ldexpf(1.f, -nsq);
-    const float sa2 = -ldexpf(1.f, -2 * nsq);    // A2s = -P * 4^-s
+    __syncwarp();
+  } else {
+    // -------------------------------------------------------- compute warps
+    const int g = warp & 3, q = warp >> 2;
+    const int r = g * 32 + lid;                          // this thread's row
+    const int c0 = q * CW;                               // ... and its first column
+    const bool row_ok = r < DP;
+    const uint32_t lane = static_cast<uint32_t>(g * 32) << 16;
+    const float es = p.edge_scale;
+    const float x1 = kT8tc[0], x2 = kT8tc[1], x3 = kT8tc[2], x4 = kT8tc[3], x5 = kT8tc[4],
+                x6 = kT8tc[5], x7 = kT8tc[6], y2 = kT8tc[7];
+    const float c2 = y2 + x3 * x4;
 
-    // ---- P2: X = A2s rows, Y^T = T1^T = -x1 As + x2 A2s rows; Q = A4 -------------
+    auto stage_gen = [&](int s) { return reinterpret_cast<float*>(stage_base + s * L::kStage); };
+    auto stage_qkv = [&](int s) { return stage_base + s * L::kStage + L::kGenBytes; };
+    auto fetch = [&](int s, int t) {        // thread 0: a_t and (q, k, v)_t into stage s
+      const long long row = ((long long)b * p.T + t) * p.H + h;
+      mbar_arrive_expect_tx(&bar_a[s], (uint32_t)(L::kGenBytes + kQkvBytes));
+      bulk_load(stage_gen(s), p.a + row * m, L::kGenBytes, &bar_a[s]);
+      bulk_load(stage_qkv(s), static_cast<const uint8_t*>(p.qkv) + row * (long long)kQkvBytes,
+                kQkvBytes, &bar_a[s]);
+    };
+    uint32_t ph_a[2] = {0, 0};
+    uint32_t pend = 0;                      // thread 0: stages with a copy in flight
+    auto wait_stage = [&](int s) {
+      bad |= !mbar_wait_abortable(&bar_a[s], ph_a[s], s_abort);
+      ph_a[s] ^= 1;
+      pend &= ~(1u << s);
+    };
+    // the generator bias of this chain's head (read through the cache: every
+    // CTA of the head reads the same m floats)
+    const float* bias_h = p.a_bias != nullptr ? p.a_bias + (long long)h * m : nullptr;
+    // A(t) from stage s -> TMEM cA and X (tf32 hi, lo).  First the packed upper
+    // triangle (plus bias, times edge_scale) is expanded into the transpose
+    // scratch, U[row][col] = a[S_row + col - row - 1] with S_row = row (2d - row - 1) / 2;
+    // then every thread reads its row segment, A[r][c] = U[r][c] (c > r),
+    // -U[c][r] (c < r), 0 (c = r).
+    auto build_a = [&](int s) {
+      const float* av = stage_gen(s);
+      for (int row = warp; row < DP - 1; row += NW) {      // a warp per row, lanes along it
+        const int base = row * (2 * DP - row - 1) / 2 - row - 1;
+        for (int col = row + 1 + lid; col < DP; col += 32) {
+          const float bv = bias_h != nullptr ? __ldg(bias_h + base + col) : 0.f;
+          XT[row * (DP + 1) + col] = __fmul_rn(av[base + col] + bv, es);
+        }
+      }
+      named_sync(kNamed, NT);
 #pragma unroll
-    for (int j = 0; j < NCH; ++j) {
-      float a2[8], a[8];
-      tmem_ld8(cP + lane + c0 + 8 * j, a2);
-      tmem_ld8(cA + lane + c0 + 8 * j, a);
-      tmem_wait_ld();
-      if (row_ok) {
-        float t1v[8];
+      for (int j = 0; j < NCH; ++j) {
+        float v[8];
+        const int rr = row_ok ? r : 0;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          a2[i] *= sa2;
-          t1v[i] = x2 * a2[i] - x1 * (a[i] * sa);
+          const int c = c0 + 8 * j + i;
+          const float up = XT[rr * (DP + 1) + c];
+          const float lo = XT[c * (DP + 1) + rr];
+          v[i] = (row_ok && c > r) ? up : ((row_ok && c < r) ? -lo : 0.f);
         }
-        put_row8<DP>(Xhi, Xlo, r, c0 + 8 * j, a2);
-        put_row8<DP>(Yhi, Ylo, r, c0 + 8 * j, t1v);
+        tmem_st8(cA + lane + c0 + 8 * j, v);
+        if (row_ok) put_row8<DP>(Xhi, Xlo, r, c0 + 8 * j, v);
+        hand_over(&ops_p1[j], lid);                       // P1 may start on this chunk
+      }
+      tmem_wait_st();
+    };
+    auto ld_rows = [&](uint32_t col, float (&v)[NCH][8]) {
+#pragma unroll
+      for (int j = 0; j < NCH; ++j) tmem_ld8(col + lane + c0 + 8 * j, v[j]);
+    };
+    uint32_t ph_p1 = 0, ph_mma = 0, ph_p4 = 0;
+    auto wait_done = [&](uint64_t* bar, uint32_t& ph) {
+      bad |= !mbar_wait_abortable(bar, ph, s_abort);
+      ph ^= 1;
+      tc_fence_after();
+    };
+
+    // ---- prologue: stages for t0 (and t0 + 1), R = I, U = (q, k, v), A(t0)
+    if (tid == 0) {
+      fetch(0, t0);
+      pend |= 1u;
+      if (t0 + 1 < t1) { fetch(1, t0 + 1); pend |= 2u; }
+    }
+    wait_stage(0);
+    {
+      const long long pos = (long long)chain * p.T + t0;
+      float* Rg = p.R + pos * DP * DP;
+      for (int i = tid; i < DP * DP; i += NT) Rg[i] = (i / DP == i % DP) ? 1.f : 0.f;
+      float* Ug = p.U + pos * 3 * DP;
+      const uint8_t* qv = stage_qkv(0);
+      for (int i = tid; i < 3 * DP; i += NT)
+        Ug[i] = QB16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(qv)[i])
+                     : reinterpret_cast<const float*>(qv)[i];
+#pragma unroll
+      for (int j = 0; j < NCH; ++j) {
+        float v[8], z[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) { v[i] = (c0 + 8 * j + i == r) ? 1.f : 0.f; z[i] = 0.f; }
+        tmem_st8(cRhi + lane + c0 + 8 * j, v);
+        tmem_st8(cRlo + lane + c0 + 8 * j, z);
       }
     }
-    operand_barrier();
-    if (tid == 0 && !bad) {
-      issue_ss<DP>(cQ, sXhi, sXlo, sYhi, sYlo);
-      tc_commit(bar_mma);
-    }
-    bad |= !mbar_wait(bar_mma, ph_mma);
-    ph_mma ^= 1;
-    tc_fence_after();
+    build_a(0);
 
-    // ---- A4 -> transpose scratch, so that each thread can read its part of A4^T
-    {
-      float a4[NCH][8];
-#pragma unroll
-      for (int j = 0; j < NCH; ++j) tmem_ld8(cQ + lane + c0 + 8 * j, a4[j]);
-      tmem_wait_ld();
-      if (row_ok) {
+    for (int t = t0; t < t1; ++t) {
+      const int it = t - t0;
+      const int sidx = it & 1, par = it & 1;
+      const bool last = (t + 1 == t1);
+
+      // ---- theta^2 <= sum over column groups of the max row abs-sum of -A^2
+      wait_done(done_p1, ph_p1);
+      float a2s[NCH][8];
+      int nsq;                  // same value in every thread (from the same maxima)
+      {
+        float av[NCH][8];
+        ld_rows(cQ, a2s);
+        ld_rows(cA, av);
+        tmem_wait_ld();
+        float rs = 0.f;
 #pragma unroll
         for (int j = 0; j < NCH; ++j)
 #pragma unroll
-          for (int i = 0; i < 8; ++i) XT[r * (DP + 1) + c0 + 8 * j + i] = a4[j][i];
-      }
-    }
-    __syncthreads();
-
-    // ---- P3: X = L rows, Y^T = F^T rows; N0 = As + (y2 + x3 x4) A2s + x4 A4 -> P
+          for (int i = 0; i < 8; ++i) rs += fabsf(a2s[j][i]);
+        if (!row_ok) rs = 0.f;
 #pragma unroll
-    for (int j = 0; j < NCH; ++j) {
-      float a2[8], a4[8], a[8], n0[8];
-      tmem_ld8(cP + lane + c0 + 8 * j, a2);
-      tmem_ld8(cQ + lane + c0 + 8 * j, a4);
-      tmem_ld8(cA + lane + c0 + 8 * j, a);
-      tmem_wait_ld();
-      if (row_ok) {
-        float lv[8], fv[8];
+        for (int o = 16; o > 0; o >>= 1) rs = fmaxf(rs, __shfl_xor_sync(0xffffffffu, rs, o));
+        if (lid == 0) atomicMax(&smax[par * 4 + q], __float_as_int(rs));   // rs >= 0
+        if (named_sync_or(kNamed, NT, bad || *s_abort != 0)) { bad = true; break; }
+        float th2 = 0.f;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int col = c0 + 8 * j + i;
-          const float a2s = a2[i] * sa2;
-          const float as = a[i] * sa;
-          const float a4t = XT[col * (DP + 1) + r];               // A4^T[r][col] = A4[col][r]
-          lv[i] = x3 * a2s + a4[i];
-          fv[i] = x6 * a2s + x7 * a4t - x5 * as;
-          n0[i] = as + (y2 + x3 * x4) * a2s + x4 * a4[i];
-        }
-        put_row8<DP>(Xhi, Xlo, r, c0 + 8 * j, lv);
-        put_row8<DP>(Yhi, Ylo, r, c0 + 8 * j, fv);
-      } else {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) n0[i] = 0.f;
-      }
-      tmem_st8(cP + lane + c0 + 8 * j, n0);
-    }
-    tmem_wait_st();
-    operand_barrier();
-    if (tid == 0 && !bad) {
-      issue_ss<DP>(cQ, sXhi, sXlo, sYhi, sYlo);        // Q = L F
-      tc_commit(bar_mma);
-    }
-    bad |= !mbar_wait(bar_mma, ph_mma);
-    ph_mma ^= 1;
-    tc_fence_after();
-
-    // ---- N = G - I = N0 + L F, then s squarings N <- 2N + N N; N rows -> Y ------
-#pragma unroll
-    for (int j = 0; j < NCH; ++j) {
-      float n0[8], nv[8];
-      tmem_ld8(cP + lane + c0 + 8 * j, n0);
-      tmem_ld8(cQ + lane + c0 + 8 * j, nv);
-      tmem_wait_ld();
-      if (row_ok) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) nv[i] += n0[i];
-        if (nsq > 0) {
-#pragma unroll
-          for (int i = 0; i < 8; ++i) XT[r * (DP + 1) + c0 + 8 * j + i] = nv[i];
-        } else {
-          put_row8<DP>(Yhi, Ylo, r, c0 + 8 * j, nv);
-        }
-      }
-    }
-    for (int sq = 0; sq < nsq; ++sq) {      // N <- 2N + N N: X = N rows, Y^T = N^T rows
-      __syncthreads();                       // N complete in the scratch
-      if (row_ok) {
+        for (int qq = 0; qq < CQ; ++qq) th2 += __int_as_float(smax[par * 4 + qq]);
+        if (tid < 4) smax[(par ^ 1) * 4 + tid] = 0;
+        nsq = 0;
+        float theta = sqrtf(th2);
+        while (theta > kTheta8tc && nsq < 64) { theta *= 0.5f; ++nsq; }
+        if (tid == 0) *s_nsq = nsq;
+        const float sa = ldexpf(1.f, -nsq);
+        const float sa2 = -ldexpf(1.f, -2 * nsq);        // A2s = -Q * 4^-s
+        // ---- P2 operands: X = A2s rows, Y^T = T1^T = -x1 As + x2 A2s rows
 #pragma unroll
         for (int j = 0; j < NCH; ++j) {
-          float nv[8], nt[8];
+          float t1v[8];
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
-            nv[i] = XT[r * (DP + 1) + c0 + 8 * j + i];
-            nt[i] = XT[(c0 + 8 * j + i) * (DP + 1) + r];
+            a2s[j][i] *= sa2;
+            t1v[i] = x2 * a2s[j][i] - x1 * (av[j][i] * sa);
           }
-          put_row8<DP>(Xhi, Xlo, r, c0 + 8 * j, nv);
-          put_row8<DP>(Yhi, Ylo, r, c0 + 8 * j, nt);
+          if (row_ok) {
+            put_row8<DP>(Xhi, Xlo, r, c0 + 8 * j, a2s[j]);
+            put_row8<DP>(Yhi, Ylo, r, c0 + 8 * j, t1v);
+          }
+          hand_over(&ops_main[j], lid);
         }
       }
-      operand_barrier();
-      if (tid == 0 && !bad) {
-        issue_ss<DP>(cQ, sXhi, sXlo, sYhi, sYlo);
-        tc_commit(bar_mma);
-      }
-      bad |= !mbar_wait(bar_mma, ph_mma);
-      ph_mma ^= 1;
-      tc_fence_after();
+      const float sa = ldexpf(1.f, -nsq);
+
+      // ---- while P2 runs: R_t and U_t to global (t > t0; R_t^T row r is in TMEM)
+      if (t > t0) {
+        const long long pos = (long long)chain * p.T + t;
+        float* Rg = p.R + pos * DP * DP;
+        const uint8_t* qv = stage_qkv(sidx);
+        float u0 = 0.f, u1 = 0.f, u2 = 0.f;
 #pragma unroll
-      for (int j = 0; j < NCH; ++j) {
-        float nv[8];
-        tmem_ld8(cQ + lane + c0 + 8 * j, nv);
+        for (int j = 0; j < NCH; ++j) {
+          float rh[1][8], rl[1][8];
+          tmem_ld8(cRhi + lane + c0 + 8 * j, rh[0]);
+          tmem_ld8(cRlo + lane + c0 + 8 * j, rl[0]);
+          tmem_wait_ld();
+          float qa[8], ka[8], va[8];
+          load8<QB16>(qv, c0 + 8 * j, qa);
+          load8<QB16>(qv, DP + c0 + 8 * j, ka);
+          load8<QB16>(qv, 2 * DP + c0 + 8 * j, va);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float v = rh[0][i] + rl[0][i];        // R_t[k][r], k = c0 + 8j + i
+            if (row_ok) Rg[(long long)(c0 + 8 * j + i) * DP + r] = v;
+            u0 = fmaf(v, qa[i], u0);
+            u1 = fmaf(v, ka[i], u1);
+            u2 = fmaf(v, va[i], u2);
+          }
+        }
+        sU[(q * 3 + 0) * 128 + r] = u0;
+        sU[(q * 3 + 1) * 128 + r] = u1;
+        sU[(q * 3 + 2) * 128 + r] = u2;
+      }
+
+      // ---- A4 = A2s T1 -> transpose scratch
+      wait_done(done_mma, ph_mma);
+      {
+        float a4[NCH][8];
+        ld_rows(cQ, a4);
         tmem_wait_ld();
         if (row_ok) {
 #pragma unroll
-          for (int i = 0; i < 8; ++i) nv[i] = fmaf(2.f, XT[r * (DP + 1) + c0 + 8 * j + i], nv[i]);
-          if (sq + 1 < nsq) {
+          for (int j = 0; j < NCH; ++j)
 #pragma unroll
-            for (int i = 0; i < 8; ++i) XT[r * (DP + 1) + c0 + 8 * j + i] = nv[i];
-          } else {
-            put_row8<DP>(Yhi, Ylo, r, c0 + 8 * j, nv);
-          }
+            for (int i = 0; i < 8; ++i) XT[r * (DP + 1) + c0 + 8 * j + i] = a4[j][i];
         }
       }
-    }
-    operand_barrier();
-
-    // ---- P4: P = R^T N^T (issued; its readout overlaps the next position's P1)
-    if (tid == 0 && !bad) {
-      issue_ts<DP>(cP, cRhi, cRlo, sYhi, sYlo);
-      tc_commit(bar_mma);
-    }
-
-    // ---- next position: A(t+1) -> X and TMEM, P1(t+1) -> Q (queued behind P4)
-    if (!last) {
-      wait_stage(sidx ^ 1);
-      add_bias(sidx ^ 1);
-      __syncthreads();
-      build_a(sidx ^ 1);
-      operand_barrier();
-      if (tid == 0 && !bad) {
-        issue_ss<DP>(cQ, sXhi, sXlo, sXhi, sXlo);
-        tc_commit(bar_p1);
-      }
-    }
-
-    // ---- R_{t+1}^T = R^T + P (R^T = hi + lo exactly); write R_{t+1} and U_{t+1},
-    //      or the chunk total after the chunk's last edge.
-    bad |= !mbar_wait(bar_mma, ph_mma);
-    ph_mma ^= 1;
-    tc_fence_after();
-    const long long pos1 = (long long)chain * p.T + t + 1;
-    float* Rg = last ? p.M + ((long long)chain * p.K + kc) * DP * DP : p.R + pos1 * DP * DP;
-    const uint8_t* qv = stage_qkv(sidx ^ 1);
-    float u0 = 0.f, u1 = 0.f, u2 = 0.f;
-#pragma unroll
-    for (int j = 0; j < NCH; ++j) {
-      float rh[8], rl[8], dv[8];
-      tmem_ld8(cRhi + lane + c0 + 8 * j, rh);
-      tmem_ld8(cRlo + lane + c0 + 8 * j, rl);
-      tmem_ld8(cP + lane + c0 + 8 * j, dv);
-      tmem_wait_ld();
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float v = (rh[i] + rl[i]) + dv[i];
-        rh[i] = to_tf32(v);
-        rl[i] = v - rh[i];
-        dv[i] = v;
-      }
-      tmem_st8(cRhi + lane + c0 + 8 * j, rh);
-      tmem_st8(cRlo + lane + c0 + 8 * j, rl);
-      if (row_ok) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int k = c0 + 8 * j + i;                 // dv[i] = R_{t+1}[k][r]
-          Rg[(long long)k * DP + r] = dv[i];
-          if (!last) {
-            u0 = fmaf(dv[i], load_elem(qv, k, p.qkv_dtype), u0);
-            u1 = fmaf(dv[i], load_elem(qv, DP + k, p.qkv_dtype), u1);
-            u2 = fmaf(dv[i], load_elem(qv, 2 * DP + k, p.qkv_dtype), u2);
-          }
-        }
-      }
-    }
-    tmem_wait_st();
-    if (!last) {                                         // U_{t+1}: sum the column groups
-      XT[(q * 3 + 0) * 128 + r] = u0;
-      XT[(q * 3 + 1) * 128 + r] = u1;
-      XT[(q * 3 + 2) * 128 + r] = u2;
-      __syncthreads();
-      if (q == 0 && row_ok) {
+      named_sync(kNamed, NT);
+      if (t > t0 && q == 0 && row_ok) {                   // U_t: sum the column groups
         float s0 = 0.f, s1 = 0.f, s2 = 0.f;
 #pragma unroll
         for (int qq = 0; qq < CQ; ++qq) {
-          s0 += XT[(qq * 3 + 0) * 128 + r];
-          s1 += XT[(qq * 3 + 1) * 128 + r];
-          s2 += XT[(qq * 3 + 2) * 128 + r];
+          s0 += sU[(qq * 3 + 0) * 128 + r];
+          s1 += sU[(qq * 3 + 1) * 128 + r];
+          s2 += sU[(qq * 3 + 2) * 128 + r];
         }
-        float* Ug = p.U + pos1 * 3 * DP;
+        float* Ug = p.U + ((long long)chain * p.T + t) * 3 * DP;
         Ug[r] = s0;
         Ug[DP + r] = s1;
         Ug[2 * DP + r] = s2;
       }
+      if (tid == 0 && t + 2 < t1) {                       // stage sidx is free: position t + 2
+        fence_proxy_async_smem();
+        fetch(sidx, t + 2);
+        pend |= 1u << sidx;
+      }
+
+      // ---- P3 operands: X = L rows, Y^T = F^T rows; N0 = As + c2 A2s + x4 A4 -> cA.
+      //      A4 comes from the scratch copy, not from Q: P3 starts overwriting Q
+      //      as soon as the first chunk is handed over.
+      {
+#pragma unroll
+        for (int j = 0; j < NCH; ++j) {
+          float av[8], n0[8];
+          tmem_ld8(cA + lane + c0 + 8 * j, av);
+          tmem_wait_ld();
+          if (row_ok) {
+            float lv[8], fv[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int col = c0 + 8 * j + i;
+              const float as = av[i] * sa;
+              const float a4 = XT[r * (DP + 1) + col];
+              const float a4t = XT[col * (DP + 1) + r];             // A4^T[r][col] = A4[col][r]
+              lv[i] = x3 * a2s[j][i] + a4;
+              fv[i] = x6 * a2s[j][i] + x7 * a4t - x5 * as;
+              n0[i] = as + c2 * a2s[j][i] + x4 * a4;
+            }
+            put_row8<DP>(Xhi, Xlo, r, c0 + 8 * j, lv);
+            put_row8<DP>(Yhi, Ylo, r, c0 + 8 * j, fv);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) n0[i] = 0.f;
+          }
+          tmem_st8(cA + lane + c0 + 8 * j, n0);
+          hand_over(&ops_main[j], lid);
+        }
+        tmem_wait_st();
+      }
+
+      // ---- N = G - I = N0 + L F, then nsq squarings N <- 2N + N N; N rows -> Y
+      wait_done(done_mma, ph_mma);
+      {
+        float n0[NCH][8], nv[NCH][8];
+        ld_rows(cA, n0);
+        ld_rows(cQ, nv);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < NCH; ++j)
+#pragma unroll
+          for (int i = 0; i < 8; ++i) nv[j][i] += n0[j][i];
+        if (nsq == 0) {
+#pragma unroll
+          for (int j = 0; j < NCH; ++j) {
+            if (row_ok) put_row8<DP>(Yhi, Ylo, r, c0 + 8 * j, nv[j]);
+            hand_over(&ops_main[j], lid);                 // P4 may start on this chunk
+          }
+        } else {
+          for (int sq = 0; sq < nsq; ++sq) {
+            if (row_ok) {
+#pragma unroll
+              for (int j = 0; j < NCH; ++j)
+#pragma unroll
+                for (int i = 0; i < 8; ++i) XT[r * (DP + 1) + c0 + 8 * j + i] = nv[j][i];
+            }
+            named_sync(kNamed, NT);                       // N complete in the scratch
+            if (row_ok) {                                 // X = N rows, Y^T = N^T rows
+#pragma unroll
+              for (int j = 0; j < NCH; ++j) {
+                float nt[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) nt[i] = XT[(c0 + 8 * j + i) * (DP + 1) + r];
+                put_row8<DP>(Xhi, Xlo, r, c0 + 8 * j, nv[j]);
+                put_row8<DP>(Yhi, Ylo, r, c0 + 8 * j, nt);
+              }
+            }
+#pragma unroll
+            for (int j = 0; j < NCH; ++j) hand_over(&ops_main[j], lid);
+            wait_done(done_mma, ph_mma);
+            float dq[NCH][8];
+            ld_rows(cQ, dq);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < NCH; ++j)
+#pragma unroll
+              for (int i = 0; i < 8; ++i) nv[j][i] = fmaf(2.f, nv[j][i], dq[j][i]);
+          }
+          if (row_ok) {
+#pragma unroll
+            for (int j = 0; j < NCH; ++j) put_row8<DP>(Yhi, Ylo, r, c0 + 8 * j, nv[j]);
+          }
+#pragma unroll
+          for (int j = 0; j < NCH; ++j) hand_over(&ops_main[j], lid);
+        }
+      }
+
+      // ---- while P4 runs: A(t+1) -> cA and X, then P1(t+1) is queued
+      if (!last) {
+        wait_stage(sidx ^ 1);
+        build_a(sidx ^ 1);
+      }
+
+      // ---- while P1(t+1) runs: R_{t+1}^T = R^T + P (R^T = hi + lo exactly) in TMEM,
+      //      or the chunk total after the chunk's last edge
+      wait_done(done_p4, ph_p4);
+      {
+        float* Mg = p.M + ((long long)chain * p.K + kc) * DP * DP;
+#pragma unroll
+        for (int j = 0; j < NCH; ++j) {
+          float rh[8], rl[8], dv[8];
+          tmem_ld8(cRhi + lane + c0 + 8 * j, rh);
+          tmem_ld8(cRlo + lane + c0 + 8 * j, rl);
+          tmem_ld8(cP + lane + c0 + 8 * j, dv);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float v = (rh[i] + rl[i]) + dv[i];
+            rh[i] = to_tf32(v);
+            rl[i] = v - rh[i];
+            if (last && row_ok) Mg[(long long)(c0 + 8 * j + i) * DP + r] = v;
+          }
+          tmem_st8(cRhi + lane + c0 + 8 * j, rh);
+          tmem_st8(cRlo + lane + c0 + 8 * j, rl);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+      }
     }
-    tc_fence_before();
+    // copies still in flight (only after an abort) land before the CTA exits
+    if (tid == 0) {
+      if (pend & 1u) bad |= !mbar_wait(&bar_a[0], ph_a[0]);
+      if (pend & 2u) bad |= !mbar_wait(&bar_a[1], ph_a[1]);
+    }
   }
 
-  bad = __syncthreads_or(bad);
+  bad = __syncthreads_or(bad || *s_abort != 0);
   if (bad && tid == 0 && p.status != nullptr) atomicExch(p.status, HOA_ERR_TIMEOUT);
   tc_fence_after();
   if (warp == 0) tmem_dealloc(tbase, L::kTmemCols);
 }
 
-template <int DP>
+template <int DP, bool QB16>
 int launch_link_tc(const LinkTcArgs& a, cudaStream_t s) {
   using L = LtLayout<DP>;
-  if (cudaFuncSetAttribute(link_tc_kernel<DP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  if (cudaFuncSetAttribute(link_tc_kernel<DP, QB16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            L::kAlloc) != cudaSuccess)
     return HOA_ERR_LAUNCH;
   const long long units = (long long)a.B * a.H * a.K;
-  link_tc_kernel<DP><<<(unsigned)units, L::NT, L::kAlloc, s>>>(a);
+  link_tc_kernel<DP, QB16><<<(unsigned)units, L::NTHREADS, L::kAlloc, s>>>(a);
   return launch_status();
+}
+
+template <int DP>
+int launch_link_tc_dt(const LinkTcArgs& a, int qkv_dtype, cudaStream_t s) {
+  return qkv_dtype == HOA_BF16 ? launch_link_tc<DP, true>(a, s) : launch_link_tc<DP, false>(a, s);
 }
 
 // Entry used by hoa_link_local: returns HOA_ERR_UNSUPPORTED when this variant
@@ -592,16 +682,16 @@ int launch_link_tc(const LinkTcArgs& a, cudaStream_t s) {
 int link_local_tc(const void* a_all, int a_dtype, const float* a_bias, float edge_scale, const void* qkv,
                   int qkv_dtype, float* R, float* U, float* M, int* status, int B, int H, int T,
                   int d, int chunk, cudaStream_t s) {
-  if (a_dtype != HOA_F32 || (reinterpret_cast<uintptr_t>(a_all) & 15) != 0 ||
-      (reinterpret_cast<uintptr_t>(qkv) & 15) != 0)
+  if (a_dtype != HOA_F32 || (qkv_dtype != HOA_F32 && qkv_dtype != HOA_BF16) ||
+      (reinterpret_cast<uintptr_t>(a_all) & 15) != 0 || (reinterpret_cast<uintptr_t>(qkv) & 15) != 0)
     return HOA_ERR_UNSUPPORTED;
-  LinkTcArgs a{static_cast<const float*>(a_all), a_bias, edge_scale, qkv, qkv_dtype, R, U, M, status,
+  LinkTcArgs a{static_cast<const float*>(a_all), a_bias, edge_scale, qkv, R, U, M, status,
                B, H, T, chunk, ceil_div(T, chunk)};
   switch (d) {
-    case 32: return launch_link_tc<32>(a, s);
-    case 48: return launch_link_tc<48>(a, s);
-    case 64: return launch_link_tc<64>(a, s);
-    case 96: return launch_link_tc<96>(a, s);
+    case 32: return launch_link_tc_dt<32>(a, qkv_dtype, s);
+    case 48: return launch_link_tc_dt<48>(a, qkv_dtype, s);
+    case 64: return launch_link_tc_dt<64>(a, qkv_dtype, s);
+    case 96: return launch_link_tc_dt<96>(a, qkv_dtype, s);
     default: return HOA_ERR_UNSUPPORTED;
   }
 }

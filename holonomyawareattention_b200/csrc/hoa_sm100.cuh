@@ -66,6 +66,46 @@ HOA_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity) {
   }
 }
 
+// The same bounded wait, which also gives up as soon as *abort is non-zero
+// and raises *abort itself when it times out, so that every other waiter of
+// the CTA stops promptly too.
+HOA_DEVICE bool mbar_wait_abortable(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort != 0) return false;
+    if (globaltimer_ns() - t0 > kMaxWaitNs) {
+      *abort = 1;
+      return false;
+    }
+  }
+}
+
+// Plain arrive (release at CTA scope) on an mbarrier.
+HOA_DEVICE void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Named barrier among `nthreads` threads (a multiple of 32).
+HOA_DEVICE void named_sync(uint32_t id, uint32_t nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// Named barrier that also returns the OR of `pred` over the participants.
+HOA_DEVICE bool named_sync_or(uint32_t id, uint32_t nthreads, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0;
+}
+
 // ---- TMA ---------------------------------------------------------------------
 HOA_DEVICE void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z) {
   asm volatile(
@@ -264,9 +304,9 @@ HOA_DEVICE void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" :
 
 // Round to tf32 (nearest, ties away), returned in an fp32 container.
 HOA_DEVICE float to_tf32(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return __uint_as_float(r);
+  // round to nearest, ties away from zero, on the magnitude bits (finite x):
+  // add half a tf32 unit in the last place, clear the 13 low bits
+  return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
 }
 
 }  // namespace sm100

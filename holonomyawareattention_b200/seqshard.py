@@ -109,7 +109,7 @@ def sequence_sharded_forward(mod, x_shard: torch.Tensor, group=None) -> torch.Te
     dtype = x_shard.dtype
     x_next = next_shard_first_token(x_shard, group)
     qkv = mod.qkv(x_shard).contiguous()
-    a, a_bias = mod._edge_generators_nobias(x_shard, x_next)
+    a, a_bias = mod._edge_generators_nobias(x_shard, x_next, seq_len=world * S)
     chunk = mod.chunk or ops.plan_chunk(B, H, S, d, x_shard.device)
     R, U, M = ops.link_local(a.contiguous(), qkv, H, mod.edge_scale, chunk, a_bias)
     del a

@@ -55,3 +55,21 @@ def test_unsupported_inputs_raise():
         inert(x, attn_mask=tril)
     with torch.no_grad(), pytest.raises(NotImplementedError, match="geometry"):
         m(x, attn_mask=tril, return_geometry=True)
+
+
+def test_generator_precision_policy():
+    """"auto" runs the bf16 edge MLP unsplit up to 8192 positions and split beyond;
+    shards of a longer sequence follow the whole sequence's length."""
+    m = PathOrderedGeometricMHA(192, n_heads=4)
+    assert m.generator_precision == "auto"
+    assert not m._split_generators(4096)
+    assert not m._split_generators(m.AUTO_SPLIT_ABOVE)
+    assert m._split_generators(m.AUTO_SPLIT_ABOVE + 1)
+    assert m._split_generators(None)
+    m.generator_precision = "split"
+    assert m._split_generators(128)
+    m.generator_precision = "bf16"
+    assert not m._split_generators(65536)
+    m.generator_precision = "fp8"
+    with pytest.raises(ValueError):
+        m._split_generators(128)

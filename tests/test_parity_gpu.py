@@ -132,13 +132,16 @@ def test_config2_full_size(dtype):
     assert O.rel_l2(y, ref) <= (FP32_TOL if dtype == torch.float32 else BF16_TOL)
 
 
-def test_config3_slice_bf16():
-    """configs[2] shape (T=4096, d_model=1536, H=16, bf16) on two batch rows vs fp32 torch restatement."""
+@pytest.mark.parametrize("precision", ["auto", "split"])
+def test_config3_slice_bf16(precision):
+    """configs[2] shape (T=4096, d_model=1536, H=16, bf16) on two batch rows vs fp32 torch
+    restatement, with the default generator precision (bf16 at this length) and the split one."""
     B, T, D, H, es = 2, 4096, 1536, 16, 0.05
     sd, x = seeded_case(D, H, seed=0, B=B, L=T, bf16_round=True)
     m = PathOrderedGeometricMHA(D, n_heads=H, edge_scale=es)
     m.load_state_dict(sd)
     m = m.to(DEV, torch.bfloat16).eval()
+    m.generator_precision = precision
     y = run(m, x.to(DEV, torch.bfloat16))
     ref = torch_ref.module_forward(sd, x.to(DEV), H, es, torch.float32, batch_slice=1).cpu().numpy()
     err = O.rel_l2(y, ref)
