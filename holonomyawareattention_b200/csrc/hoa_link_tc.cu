@@ -28,6 +28,8 @@
 // into a double-buffered stage; the next position's A-build and its P1 run
 // while the current composition P4 and its readout complete (two commit
 // barriers, alternating TMEM roles).
+#include <utility>
+
 #include "hoa_sm100.cuh"
 
 namespace hoa {
@@ -118,41 +120,50 @@ HOA_DEVICE void put_row8(uint8_t* hi_buf, uint8_t* lo_buf, int row, int c0, cons
 
 // One 8-column chunk j of every column group (K-steps q * NCH + j) of a 3-pass
 // SS product D = X Y, X given as rows and Y as the rows of Y^T (both K-major,
-// 128B-swizzled).  Chunk 0 (q = 0, first pass) starts the accumulation.
-template <int DP>
-HOA_DEVICE void issue_ss_chunk(uint32_t d_tmem, uint32_t xhi, uint32_t xlo, uint32_t yhi, uint32_t ylo,
-                               int j) {
+// 128B-swizzled).  Chunk 0 (q = 0, first pass) starts the accumulation.  The
+// operands come as base descriptors: a K-step's descriptor is the base plus
+// its byte offset / 16 (the start-address field cannot carry: shared
+// addresses stay below 2^18).
+template <int DP, int J>
+HOA_DEVICE void issue_ss_chunk(uint32_t d_tmem, uint64_t xhi, uint64_t xlo, uint64_t yhi, uint64_t ylo) {
   using L = LtLayout<DP>;
   constexpr uint32_t id = make_idesc(kFmtTF32, 128, DP);
-  const uint32_t xs[3] = {xhi, xhi, xlo};
-  const uint32_t ys[3] = {yhi, ylo, yhi};
 #pragma unroll
   for (int q = 0; q < L::CQ; ++q) {
-    const int kk = q * L::NCH + j;
-    const uint32_t off = (kk >> 2) * L::kSlab + (kk & 3) * 32;
-#pragma unroll
-    for (int ps = 0; ps < 3; ++ps)
-      mma_tf32(d_tmem, desc_sw128(xs[ps] + off), desc_sw128(ys[ps] + off), id, (j | q | ps) ? 1u : 0u);
+    constexpr int kNch = L::NCH;
+    const int kk = q * kNch + J;
+    const uint64_t off = (uint64_t)(((kk >> 2) * L::kSlab + (kk & 3) * 32) >> 4);
+    mma_tf32(d_tmem, xhi + off, yhi + off, id, (J | q) ? 1u : 0u);
+    mma_tf32(d_tmem, xhi + off, ylo + off, id, 1u);
+    mma_tf32(d_tmem, xlo + off, yhi + off, id, 1u);
   }
 }
 
 // The same for a 3-pass TS product D = A B^T: A from TMEM (hi, lo columns),
-// B rows K-major in shared memory.
-template <int DP>
-HOA_DEVICE void issue_ts_chunk(uint32_t d_tmem, uint32_t ahi, uint32_t alo, uint32_t bhi, uint32_t blo,
-                               int j) {
+// B rows K-major in shared memory (base descriptors).
+template <int DP, int J>
+HOA_DEVICE void issue_ts_chunk(uint32_t d_tmem, uint32_t ahi, uint32_t alo, uint64_t bhi, uint64_t blo) {
   using L = LtLayout<DP>;
   constexpr uint32_t id = make_idesc(kFmtTF32, 128, DP);
-  const uint32_t as[3] = {ahi, ahi, alo};
-  const uint32_t bs[3] = {bhi, blo, bhi};
 #pragma unroll
   for (int q = 0; q < L::CQ; ++q) {
-    const int kk = q * L::NCH + j;
-    const uint32_t off = (kk >> 2) * L::kSlab + (kk & 3) * 32;
-#pragma unroll
-    for (int ps = 0; ps < 3; ++ps)
-      mma_tf32_ts(d_tmem, as[ps] + kk * 8, desc_sw128(bs[ps] + off), id, (j | q | ps) ? 1u : 0u);
+    constexpr int kNch = L::NCH;
+    const int kk = q * kNch + J;
+    const uint64_t off = (uint64_t)(((kk >> 2) * L::kSlab + (kk & 3) * 32) >> 4);
+    mma_tf32_ts(d_tmem, ahi + kk * 8, bhi + off, id, (J | q) ? 1u : 0u);
+    mma_tf32_ts(d_tmem, ahi + kk * 8, blo + off, id, 1u);
+    mma_tf32_ts(d_tmem, alo + kk * 8, bhi + off, id, 1u);
   }
+}
+
+// f(std::integral_constant<int, 0>{}), ..., f(std::integral_constant<int, N - 1>{})
+template <int... Is, class F>
+HOA_DEVICE void unroll_impl(std::integer_sequence<int, Is...>, F&& f) {
+  (f(std::integral_constant<int, Is>{}), ...);
+}
+template <int N, class F>
+HOA_DEVICE void unroll(F&& f) {
+  unroll_impl(std::make_integer_sequence<int, N>{}, f);
 }
 
 // Hand-over of operands from the compute warps to the MMA warp: each thread
@@ -263,6 +274,8 @@ __global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, 1) link_tc_kernel(Link
     // ------------------------------------------------------------ MMA warp
     if (lid == 0) {
       uint32_t ph_main = 0, ph_p1 = 0;   // bit j: phase parity of barrier j of the set
+      const uint64_t dXhi = desc_sw128(sXhi), dXlo = desc_sw128(sXlo), dYhi = desc_sw128(sYhi),
+                     dYlo = desc_sw128(sYlo);
       // waits for chunk j of the set, then issues that chunk of the product
       auto wait_chunk = [&](uint64_t* set, uint32_t& ph, int j) {
         const bool ok = mbar_wait_abortable(&set[j], (ph >> j) & 1u, s_abort);
@@ -270,39 +283,39 @@ __global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, 1) link_tc_kernel(Link
         if (ok) tc_fence_after();
         return ok;
       };
-      auto product_ss = [&](uint64_t* set, uint32_t& ph, uint32_t d, uint32_t xh, uint32_t xl,
-                            uint32_t yh, uint32_t yl) {
-        for (int j = 0; j < NCH; ++j) {
-          if (!wait_chunk(set, ph, j)) return false;
-          issue_ss_chunk<DP>(d, xh, xl, yh, yl, j);
-        }
-        return true;
+      // waits for each chunk of the set in turn and issues it (issue(jc), jc a compile-time index)
+      auto product = [&](uint64_t* set, uint32_t& ph, auto&& issue) {
+        bool ok = true;
+        unroll<NCH>([&](auto jc) {
+          if (ok) {
+            ok = wait_chunk(set, ph, decltype(jc)::value);
+            if (ok) issue(jc);
+          }
+        });
+        return ok;
       };
-      bool ok = product_ss(ops_p1, ph_p1, cQ, sXhi, sXlo, sXhi, sXlo);     // Q = A A^T = -A^2
+      auto ss_xx = [&](auto jc) { issue_ss_chunk<DP, decltype(jc)::value>(cQ, dXhi, dXlo, dXhi, dXlo); };
+      auto ss_xy = [&](auto jc) { issue_ss_chunk<DP, decltype(jc)::value>(cQ, dXhi, dXlo, dYhi, dYlo); };
+      auto ts_ry = [&](auto jc) { issue_ts_chunk<DP, decltype(jc)::value>(cP, cRhi, cRlo, dYhi, dYlo); };
+      bool ok = product(ops_p1, ph_p1, ss_xx);                               // Q = A A^T = -A^2
       if (ok) tc_commit(done_p1);
       for (int t = t0; t < t1 && ok; ++t) {
         // P2 (Q = A2s T1); the squaring count is published before chunk 0's hand-over
-        if (!wait_chunk(ops_main, ph_main, 0)) break;
-        const int nsq = *s_nsq;
-        issue_ss_chunk<DP>(cQ, sXhi, sXlo, sYhi, sYlo, 0);
-        for (int j = 1; j < NCH && ok; ++j) {
-          ok = wait_chunk(ops_main, ph_main, j);
-          if (ok) issue_ss_chunk<DP>(cQ, sXhi, sXlo, sYhi, sYlo, j);
-        }
+        int nsq = 0;
+        ok = product(ops_main, ph_main, [&](auto jc) {
+          if constexpr (decltype(jc)::value == 0) nsq = *s_nsq;
+          ss_xy(jc);
+        });
         if (!ok) break;
         tc_commit(done_mma);
         for (int sq = -1; sq < nsq && ok; ++sq) {                        // Q = L F, then Q = N N
-          ok = product_ss(ops_main, ph_main, cQ, sXhi, sXlo, sYhi, sYlo);
+          ok = product(ops_main, ph_main, ss_xy);
           if (ok) tc_commit(done_mma);
         }
-        for (int j = 0; j < NCH && ok; ++j) {                            // P = R^T N^T
-          ok = wait_chunk(ops_main, ph_main, j);
-          if (ok) issue_ts_chunk<DP>(cP, cRhi, cRlo, sYhi, sYlo, j);
-        }
-        if (!ok) break;
+        if (!ok || !product(ops_main, ph_main, ts_ry)) break;            // P = R^T N^T
         tc_commit(done_p4);
         if (t + 1 < t1) {
-          ok = product_ss(ops_p1, ph_p1, cQ, sXhi, sXlo, sXhi, sXlo);
+          ok = product(ops_p1, ph_p1, ss_xx);
           if (ok) tc_commit(done_p1);
         }
       }

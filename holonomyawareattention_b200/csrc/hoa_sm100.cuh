@@ -53,16 +53,18 @@ HOA_DEVICE uint64_t globaltimer_ns() {
   return t;
 }
 
-// Bounded wait on the phase with the given parity: gives up after ~2 s of
-// wall time (each try_wait may itself suspend for a hardware-defined window,
-// so the bound is on the clock, not on the number of tries).
-constexpr uint64_t kMaxWaitNs = 2000000000ull;
+// Bounded wait on the phase with the given parity.  The bound is on the SM's
+// cycle counter (cheap to read, unlike the global nanosecond timer): 4e9
+// cycles, i.e. 2 s at 2 GHz and longer at lower clocks.  Each try_wait may
+// itself suspend for a hardware-defined window, so the bound is on the clock,
+// not on the number of tries.
+constexpr long long kMaxWaitCycles = 4000000000ll;
 HOA_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
+  const long long c0 = clock64();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (globaltimer_ns() - t0 > kMaxWaitNs) return false;
+    if (clock64() - c0 > kMaxWaitCycles) return false;
   }
 }
 
@@ -71,11 +73,11 @@ HOA_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity) {
 // the CTA stops promptly too.
 HOA_DEVICE bool mbar_wait_abortable(uint64_t* bar, uint32_t parity, volatile int* abort) {
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
+  const long long c0 = clock64();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort != 0) return false;
-    if (globaltimer_ns() - t0 > kMaxWaitNs) {
+    if (clock64() - c0 > kMaxWaitCycles) {
       *abort = 1;
       return false;
     }
