@@ -4,14 +4,9 @@
 //   s_ij = q^_i . k^_j * scale, tril mask, online softmax, o / l.clamp_min(1e-20)
 //   core/attention_fast_chunked.py:119-168
 //
-// One CTA (4 warps) per (128-query tile, chain).  Thread 0 issues the TMA loads
-// (128B-swizzled bf16 tiles of q^, k^ and v^T) and the tcgen05 MMAs; all 128
-// threads run the softmax, one query row each (TMEM lane = row):
-//   S   = Q K^T      M=128, N=128 keys, K=d     -> TMEM columns [0, 128)
-//   P   = exp2(S*scale*log2e - m) as bf16, written to shared memory (swizzled)
-//   O_j = P V        M=128, N=d (padded to 16),  K=128 keys -> TMEM columns [128, 128+d)
-//   o  <- o * exp2(m_old - m_new) + O_j  (fp32, per-row accumulator in shared memory)
-// Output: o / l in fp32, (B*H, Tq, d), consumed by the inverse transport (kernel 4).
+// One CTA per (pair of 128-query tiles, chain); the warp roles and the TMEM
+// plan are described at the kernel.  Output: o / l in fp32, (B*H, Tq, d),
+// consumed by the inverse transport (kernel 4).
 // Queries may be a shard of the sequence: local row i is global position
 // q_offset + i and attends to keys 0 .. q_offset + i of the (gathered) key set.
 #include <cudaTypedefs.h>
@@ -21,22 +16,42 @@
 namespace hoa {
 using namespace sm100;
 
-constexpr int kTcThreads = 128;
+// Warp roles (320 threads):
+//   warps 0-3  softmax of Q tile 0 (row r of the tile = TMEM lane r = thread r)
+//   warps 4-7  softmax of Q tile 1
+//   warp 8     issues the tcgen05 products (one elected lane)
+//   warp 9     issues the TMA loads: both Q tiles once, then K and V^T tiles
+//              through a 2-stage ring
+// Per key tile j, for each Q tile i (two tiles keep the tensor core busy while
+// the other tile's softmax runs):
+//   S_i = Q_i K_j^T     SS, M=128, N=128 keys, K=d      -> TMEM columns S_i
+//   P_i = exp2(S_i * scale * log2e - m_i) as bf16, written back over S_i
+//   O_i += P_i V_j      TS (P from TMEM), N=d (padded to 16), K=128 keys -> TMEM O_i
+// The reference point m_i of the exponent moves only when a row's running
+// maximum grows by more than 8 (a factor 256): then that warp rescales its
+// rows of O_i in TMEM (after the previous P V of the tile has completed) and
+// l_i.  Between moves P <= 256, exact in the sums; the result o = O / l is
+// the same softmax, with the final division by l as in the reference.
+constexpr int kFaThreads = 320;
+constexpr int kFaRescaleLog2 = 8;
 
 template <int DP16>
-struct TcLayout {
-  static constexpr int NKB = (DP16 + 63) / 64;        // 64-column blocks of the Q / K tiles
+struct FaLayout {
+  static constexpr int NKB = (DP16 + 63) / 64;        // 64-column boxes of a Q or K tile
   static constexpr int kBlk = 128 * 128;              // bytes: 128 rows x 128 B
-  static constexpr int kVblk = DP16 * 128;            // bytes per 64-key block of V^T
-  static constexpr int offQ = 0;
-  static constexpr int offK = offQ + NKB * kBlk;
-  static constexpr int offV = offK + NKB * kBlk;
-  static constexpr int offP = offV + 2 * kVblk;
-  static constexpr int offO = offP + 2 * kBlk;         // fp32 accumulator, [DP16][128 rows]
-  static constexpr int offBar = offO + DP16 * 128 * 4;
-  static constexpr int kBytes = offBar + 64;
+  static constexpr int kQ = NKB * kBlk;               // one Q (or K) tile
+  static constexpr int kVblk = DP16 * 128;            // one 64-key box of V^T
+  static constexpr int kStage = kQ + 2 * kVblk;       // K tile + V^T tile (128 keys)
+  static constexpr int NS = 2;
+  static constexpr int offQ = 0;                      // Q tiles 0 and 1
+  static constexpr int offStage = 2 * kQ;
+  static constexpr int offBar = offStage + NS * kStage;
+  static constexpr int kBytes = offBar + 256;
   static constexpr int kAlloc = kBytes + 1024;        // slack to align the base to 1024
   static_assert(kVblk % 1024 == 0, "V^T blocks must stay 1024-aligned");
+  static_assert(kAlloc <= 232448, "shared memory budget");
+  // TMEM columns: S_0, S_1 (128 each), O_0, O_1 (128 each, DP16 used)
+  static constexpr uint32_t colS0 = 0, colS1 = 128, colO0 = 256, colO1 = 384;
 };
 
 struct AttnTcArgs {
@@ -51,176 +66,223 @@ HOA_DEVICE uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<const uint32_t*>(&v);
 }
 
+// key tiles (of 128) that the query rows starting at global position gq0 see
+HOA_DEVICE int fa_key_tiles(int gq0, int Tk) { return min((gq0 + 127) / 128, (Tk - 1) / 128) + 1; }
+
 template <int DP16>
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __launch_bounds__(kFaThreads, 1)
 attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                const __grid_constant__ CUtensorMap tv, AttnTcArgs p) {
-  using L = TcLayout<DP16>;
+  using L = FaLayout<DP16>;
   extern __shared__ uint8_t smem_raw[];
   // 1024-aligned base by pointer arithmetic on the shared array, so that the
   // compiler keeps every derived pointer in the shared address space
   uint8_t* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  uint8_t* sQ = sm + L::offQ;
-  uint8_t* sK = sm + L::offK;
-  uint8_t* sV = sm + L::offV;
-  uint8_t* sP = sm + L::offP;
-  float* sO = reinterpret_cast<float*>(sm + L::offO);
-  uint64_t* bar_tma = reinterpret_cast<uint64_t*>(sm + L::offBar);
-  uint64_t* bar_mma = bar_tma + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_mma + 1);
-  const int tid = threadIdx.x, warp = tid >> 5;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::offBar);
+  uint64_t* q_full = bars + 0;
+  uint64_t* kv_full = bars + 1;      // [2]
+  uint64_t* kv_empty = bars + 3;     // [2]
+  uint64_t* s_full = bars + 5;       // [2] per Q tile
+  uint64_t* p_full = bars + 7;       // [2] per Q tile
+  uint64_t* pv_done = bars + 9;      // [2] per Q tile
+  uint64_t* fin = bars + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(bars + 13);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lid = tid & 31;
   const int chain = blockIdx.y;
-  const int qt = gridDim.x - 1 - blockIdx.x;     // heaviest causal tiles first
-  const int q0 = qt * 128;                        // local query row of this tile
-  const int Tq = p.Tq, Tk = p.Tk, d = p.d;
-  const int gq0 = p.q_offset + q0;                // global position of its first row
-  const int nkt = min((gq0 + 127) / 128, (Tk - 1) / 128) + 1;   // key tiles this tile sees
+  const int nqt = (p.Tq + 127) / 128;
+  const int pair = gridDim.x - 1 - blockIdx.x;     // heaviest causal pairs first
+  const int Tk = p.Tk;
+  int n_t[2];                                       // key tiles of each Q tile (0: absent)
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int qt = 2 * pair + i;
+    n_t[i] = qt < nqt ? fa_key_tiles(p.q_offset + qt * 128, Tk) : 0;
+  }
+  const int nkt = max(n_t[0], n_t[1]);
 
   if (tid == 0) {
-    mbar_init(bar_tma, 1);
-    mbar_init(bar_mma, 1);
+    for (int i = 0; i < 12; ++i) mbar_init(&bars[i], (i == 7 || i == 8) ? 4 : 1);
+    *s_abort = 0;
     fence_mbar_init();
   }
   if (warp == 0) {
-    tmem_alloc(tmem_slot, 256);
+    tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem;
-  const uint32_t tO = tmem + 128;
-  const uint32_t lane = static_cast<uint32_t>(warp * 32) << 16;
+  bool bad = false;
 
-  constexpr uint32_t idS = make_idesc(kFmtBF16, 128, 128);
-  constexpr uint32_t idO = make_idesc(kFmtBF16, 128, DP16);
-  constexpr int KSTEPS = DP16 / 16;
-  const uint32_t qk_bytes = L::NKB * L::kBlk;
-  const uint32_t v_bytes = 2u * 64u * (uint32_t)d * 2u;
-  uint32_t ph_tma = 0, ph_mma = 0;
-
-  if (tid == 0) {
-    mbar_arrive_expect_tx(bar_tma, qk_bytes);
-    for (int kb = 0; kb < L::NKB; ++kb) tma_load_3d(sQ + kb * L::kBlk, &tq, bar_tma, kb * 64, q0, chain);
-  }
-  // `bad` records a bounded wait that gave up; the loop is left only at its
-  // top, by a block-uniform vote, so every thread reaches the same barriers.
-  bool bad = !mbar_wait(bar_tma, ph_tma);
-  ph_tma ^= 1;
-
-  const int qi = gq0 + tid;                        // this thread's global query position
-  float m_run = -INFINITY, l_run = 0.f;
-#pragma unroll 8
-  for (int e = 0; e < DP16; ++e) sO[e * 128 + tid] = 0.f;    // this row's accumulator
-
-  for (int j = 0; j < nkt; ++j) {
-    if (__syncthreads_or(bad)) { bad = true; break; }
-    const int k0 = j * 128;
-    if (tid == 0) {
-      mbar_arrive_expect_tx(bar_tma, qk_bytes + v_bytes);
-      for (int kb = 0; kb < L::NKB; ++kb) tma_load_3d(sK + kb * L::kBlk, &tk, bar_tma, kb * 64, k0, chain);
-      tma_load_3d(sV, &tv, bar_tma, k0, 0, chain);
-      tma_load_3d(sV + L::kVblk, &tv, bar_tma, k0 + 64, 0, chain);
-    }
-    bad |= !mbar_wait(bar_tma, ph_tma);
-    ph_tma ^= 1;
-    tc_fence_after();
-    if (tid == 0 && !bad) {
-      const uint32_t qa = smem_u32(sQ), ka = smem_u32(sK);
-#pragma unroll
-      for (int kk = 0; kk < KSTEPS; ++kk) {
-        const uint32_t off = (kk >> 2) * L::kBlk + (kk & 3) * 32;
-        mma_bf16(tS, desc_sw128(qa + off), desc_sw128(ka + off), idS, kk > 0 ? 1u : 0u);
+  if (warp == 9) {
+    // ------------------------------------------------------------------ TMA
+    if (lid == 0) {
+      const uint32_t kq = L::kQ;
+      mbar_arrive_expect_tx(q_full, (n_t[1] > 0 ? 2u : 1u) * kq);
+      for (int i = 0; i < 2; ++i)
+        if (n_t[i] > 0)
+          for (int kb = 0; kb < L::NKB; ++kb)
+            tma_load_3d(sm + L::offQ + i * L::kQ + kb * L::kBlk, &tq, q_full, kb * 64,
+                        (2 * pair + i) * 128, chain);
+      const uint32_t v_bytes = 2u * 64u * (uint32_t)p.d * 2u;
+      int issued[2] = {0, 0};
+      for (int j = 0; j < nkt; ++j) {
+        const int s = j & 1;
+        if (j >= 2 && !mbar_wait_abortable(&kv_empty[s], ((j >> 1) - 1) & 1, s_abort)) { bad = true; break; }
+        uint8_t* st = sm + L::offStage + s * L::kStage;
+        mbar_arrive_expect_tx(&kv_full[s], kq + v_bytes);
+        for (int kb = 0; kb < L::NKB; ++kb) tma_load_3d(st + kb * L::kBlk, &tk, &kv_full[s], kb * 64, j * 128, chain);
+        tma_load_3d(st + L::kQ, &tv, &kv_full[s], j * 128, 0, chain);
+        tma_load_3d(st + L::kQ + L::kVblk, &tv, &kv_full[s], j * 128 + 64, 0, chain);
+        issued[s] = j + 1;
       }
-      tc_commit(bar_mma);
+      // copies in flight land before the CTA exits (the last fill of each stage)
+      for (int s = 0; s < 2; ++s)
+        if (issued[s] > 0) bad |= !mbar_wait(&kv_full[s], ((issued[s] - 1) >> 1) & 1);
+      bad |= !mbar_wait(q_full, 0);
     }
-    bad |= !mbar_wait(bar_mma, ph_mma);
-    ph_mma ^= 1;
-    tc_fence_after();
-
-    // ---- softmax over this tile's 128 keys (row qi) ------------------------
-    float mt = -INFINITY;
+    __syncwarp();
+  } else if (warp == 8) {
+    // ------------------------------------------------------------------ MMA
+    if (lid == 0) {
+      constexpr uint32_t idS = make_idesc(kFmtBF16, 128, 128);
+      constexpr uint32_t idO = make_idesc(kFmtBF16, 128, DP16);
+      constexpr int KSTEPS = DP16 / 16;
+      const uint64_t dQ[2] = {desc_sw128(smem_u32(sm + L::offQ)), desc_sw128(smem_u32(sm + L::offQ + L::kQ))};
+      const uint32_t colS[2] = {tmem + L::colS0, tmem + L::colS1};
+      const uint32_t colO[2] = {tmem + L::colO0, tmem + L::colO1};
+      bool ok = mbar_wait_abortable(q_full, 0, s_abort);
+      for (int j = 0; j < nkt && ok; ++j) {
+        const int s = j & 1;
+        ok = mbar_wait_abortable(&kv_full[s], (j >> 1) & 1, s_abort);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t st = smem_u32(sm + L::offStage + s * L::kStage);
+        const uint64_t dK = desc_sw128(st), dV = desc_sw128(st + L::kQ);
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      float v[16];
-      tmem_ld16(tS + lane + c * 16, v);
+        for (int i = 0; i < 2; ++i) {
+          if (j >= n_t[i]) continue;
+#pragma unroll
+          for (int kk = 0; kk < KSTEPS; ++kk) {
+            const uint64_t off = (uint64_t)(((kk >> 2) * L::kBlk + (kk & 3) * 32) >> 4);
+            mma_bf16(colS[i], dQ[i] + off, dK + off, idS, kk > 0 ? 1u : 0u);
+          }
+          tc_commit(&s_full[i]);
+        }
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          if (j >= n_t[i] || !ok) continue;
+          ok = mbar_wait_abortable(&p_full[i], j & 1, s_abort);
+          if (!ok) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint64_t boff = (uint64_t)(((kk >> 2) * L::kVblk + (kk & 3) * 32) >> 4);
+            mma_bf16_ts(colO[i], colS[i] + kk * 8, dV + boff, idO, (j > 0 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit(&pv_done[i]);
+        }
+        tc_commit(&kv_empty[s]);
+      }
+      if (!ok) bad = true;
+      tc_commit(fin);
+      bad |= !mbar_wait(fin, 0);
+    }
+    __syncwarp();
+  } else {
+    // -------------------------------------------------------------- softmax
+    const int i = warp >> 2;                         // Q tile of this warpgroup
+    const int r = tid & 127;                         // row in the tile = TMEM lane
+    const uint32_t lane = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t cS = tmem + (i ? L::colS1 : L::colS0) + lane;
+    const uint32_t cO = tmem + (i ? L::colO1 : L::colO0) + lane;
+    const int ni = n_t[i];
+    const int qi = p.q_offset + (2 * pair + i) * 128 + r;   // global query position
+    const float c = p.scale_log2;
+    float m_ref = -INFINITY, l_run = 0.f;
+    for (int j = 0; j < ni; ++j) {
+      bad |= !mbar_wait_abortable(&s_full[i], j & 1, s_abort);
+      tc_fence_after();
+      float sv[4][32];
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) tmem_ld32(cS + 32 * q4, sv[q4]);
       tmem_wait_ld();
+      const int k0 = j * 128;
+      const bool diag = k0 + 127 > qi || k0 + 127 >= Tk;          // some key of the tile masked
+      float mt = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int key = k0 + c * 16 + i;
-        if (key <= qi && key < Tk) mt = fmaxf(mt, v[i]);
+      for (int k = 0; k < 128; ++k) {
+        const bool ok = !diag || (k0 + k <= qi && k0 + k < Tk);
+        if (!ok) sv[k >> 5][k & 31] = -INFINITY;
+        mt = fmaxf(mt, sv[k >> 5][k & 31]);
+      }
+      const float m_cand = mt * c;
+      const bool move = m_cand > m_ref + (float)kFaRescaleLog2;    // also the first tile (m_ref = -inf)
+      const float m_new = move ? m_cand : m_ref;
+      const float corr = move ? exp2f(m_ref - m_new) : 1.f;        // 0 on the first tile
+      if (__any_sync(0xffffffffu, move) && j > 0) {
+        // rescale this warp's rows of O once the previous P V has completed
+        bad |= !mbar_wait_abortable(&pv_done[i], (j - 1) & 1, s_abort);
+        tc_fence_after();
+#pragma unroll
+        for (int c16 = 0; c16 < DP16 / 16; ++c16) {
+          float ov[16];
+          tmem_ld16(cO + 16 * c16, ov);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 16; ++e) ov[e] *= corr;
+          tmem_st16(cO + 16 * c16, ov);
+        }
+      }
+      l_run *= corr;
+      m_ref = m_new;
+      float rs = 0.f;
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {                  // 32 keys -> 16 packed columns
+        float pk[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const float p0 = exp2f(fmaf(sv[h][2 * e], c, -m_ref));
+          const float p1 = exp2f(fmaf(sv[h][2 * e + 1], c, -m_ref));
+          rs += p0 + p1;
+          pk[e] = __uint_as_float(pack_bf16x2(p0, p1));
+        }
+        tmem_st16(cS + 16 * h, pk);
+      }
+      l_run += rs;
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lid == 0) mbar_arrive(&p_full[i]);
+    }
+    // ---- epilogue: o = O / l for the rows of this tile that exist
+    if (ni > 0) {
+      bad |= !mbar_wait_abortable(&pv_done[i], (ni - 1) & 1, s_abort);
+      tc_fence_after();
+      const int lrow = (2 * pair + i) * 128 + r;     // local query row
+      const float inv = 1.f / fmaxf(l_run, 1e-20f);
+      float* orow = p.o + ((long long)chain * p.Tq + lrow) * p.d;
+#pragma unroll
+      for (int c16 = 0; c16 < DP16 / 16; ++c16) {
+        float ov[16];
+        tmem_ld16(cO + 16 * c16, ov);
+        tmem_wait_ld();
+        if (lrow < p.Tq && !bad) {
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            if (16 * c16 + e < p.d) orow[16 * c16 + e] = ov[e] * inv;
+        }
       }
     }
-    const float m_new = fmaxf(m_run, mt * p.scale_log2);
-    const float corr = exp2f(m_run - m_new);
-    float rs = 0.f;
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      float v[16];
-      tmem_ld16(tS + lane + c * 16, v);
-      tmem_wait_ld();
-      uint32_t pk[8];
-#pragma unroll
-      for (int i = 0; i < 16; i += 2) {
-        const int key = k0 + c * 16 + i;
-        const float p0 = (key <= qi && key < Tk) ? exp2f(fmaf(v[i], p.scale_log2, -m_new)) : 0.f;
-        const float p1 =
-            (key + 1 <= qi && key + 1 < Tk) ? exp2f(fmaf(v[i + 1], p.scale_log2, -m_new)) : 0.f;
-        rs += p0 + p1;
-        pk[i >> 1] = pack_bf16x2(p0, p1);
-      }
-#pragma unroll
-      for (int g = 0; g < 2; ++g) {
-        const int gg = c * 2 + g;                 // 16-byte chunk index along the 128 keys
-        uint4 val = make_uint4(pk[4 * g], pk[4 * g + 1], pk[4 * g + 2], pk[4 * g + 3]);
-        *reinterpret_cast<uint4*>(sP + (gg >> 3) * L::kBlk + sw128_offset(tid, gg & 7)) = val;
-      }
-    }
-    l_run = l_run * corr + rs;
-    m_run = m_new;
-    fence_proxy_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    if (tid == 0 && !bad) {
-      const uint32_t pa = smem_u32(sP), va = smem_u32(sV);
-#pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        const uint32_t aoff = (kk >> 2) * L::kBlk + (kk & 3) * 32;
-        const uint32_t boff = (kk >> 2) * L::kVblk + (kk & 3) * 32;
-        mma_bf16(tO, desc_sw128(pa + aoff), desc_sw128(va + boff), idO, kk > 0 ? 1u : 0u);
-      }
-      tc_commit(bar_mma);
-    }
-    bad |= !mbar_wait(bar_mma, ph_mma);
-    ph_mma ^= 1;
-    tc_fence_after();
-#pragma unroll
-    for (int c = 0; c < DP16 / 16; ++c) {
-      float v[16];
-      tmem_ld16(tO + lane + c * 16, v);
-      tmem_wait_ld();
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        float* a = sO + (c * 16 + i) * 128 + tid;
-        *a = fmaf(*a, corr, v[i]);
-      }
-    }
-    tc_fence_before();
   }
 
-  bad = __syncthreads_or(bad);
-  if (q0 + tid < Tq && !bad) {
-    const float inv = 1.f / fmaxf(l_run, 1e-20f);
-    float* orow = p.o + ((long long)chain * Tq + q0 + tid) * d;
-    for (int e = 0; e < d; ++e) orow[e] = sO[e * 128 + tid] * inv;
-  }
+  bad = __syncthreads_or(bad || *s_abort != 0);
   if (bad && tid == 0 && p.status != nullptr) atomicExch(p.status, HOA_ERR_TIMEOUT);
-  tc_fence_before();
-  __syncthreads();
   tc_fence_after();
-  if (warp == 0) tmem_dealloc(tmem, 256);
+  if (warp == 0) tmem_dealloc(tmem, 512);
 }
 
 // ---------------------------------------------------------------------------
@@ -260,12 +322,12 @@ static bool make_map(CUtensorMap* m, const void* base, uint64_t x, uint64_t y, u
 template <int DP16>
 static int launch_tc(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                      const AttnTcArgs& a, int BH, cudaStream_t s) {
-  using L = TcLayout<DP16>;
+  using L = FaLayout<DP16>;
   if (cudaFuncSetAttribute(attn_tc_kernel<DP16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            L::kAlloc) != cudaSuccess)
     return HOA_ERR_LAUNCH;
-  dim3 grid((unsigned)ceil_div(a.Tq, 128), (unsigned)BH);
-  attn_tc_kernel<DP16><<<grid, kTcThreads, L::kAlloc, s>>>(mq, mk, mv, a);
+  dim3 grid((unsigned)ceil_div(ceil_div(a.Tq, 128), 2), (unsigned)BH);
+  attn_tc_kernel<DP16><<<grid, kFaThreads, L::kAlloc, s>>>(mq, mk, mv, a);
   return launch_status();
 }
 

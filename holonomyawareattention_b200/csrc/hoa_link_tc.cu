@@ -6,28 +6,32 @@
 // (core/utils.py:4-52, core/attention_fast_chunked.py:77, 86-94, 108-110);
 // this variant serves d in {32, 48, 64, 96} with fp32 generators.
 //
-// One CTA per (chain, chunk): 4 TMEM lane groups x 4 (or 2) column groups of
-// warps; the thread at (lane group g, lane l, column group q) owns row 32g + l
-// (TMEM lane = row of every accumulator) and a quarter (or half) of its columns.  Every product D = X Y
-// takes X as rows (K-major) and Y as the rows of Y^T (K-major B operand), in
-// the 128B-swizzled layout; the matrices are polynomials in the skew A, so
+// One CTA per (chain, chunk).  Compute warps form 4 TMEM lane groups x CQ
+// column groups; the thread at (lane group g, lane l, column group q) owns row
+// 32g + l (TMEM lane = row of every accumulator) and 1/CQ of its columns.  One
+// more warp only issues the tensor-core products.  Every product D = X Y takes
+// X as rows (K-major) and Y as the rows of Y^T (K-major B operand), in the
+// 128B-swizzled layout; the matrices are polynomials in the skew A, so
 // p(A)^T = p(-A) gives most transposes for free:
-//   P1  D1 = A A^T = -A^2            X = Y^T = A rows (one buffer)
-//   P2  D2 = A2s T1 = A4             Y^T = T1^T = -x1 As + x2 A2s  (As = A 2^-s, A2s = A^2 4^-s)
-//   P3  D2 = L F                     L = x3 A2s + A4, F = x5 As + x6 A2s + x7 A4 (= Rf - x4 I);
+//   P1  Q = A A^T = -A^2             X = Y^T = A rows (one shared-memory buffer)
+//   P2  Q = A2s T1 = A4              Y^T = T1^T = -x1 As + x2 A2s  (As = A 2^-s, A2s = A^2 4^-s)
+//   P3  Q = L F                      L = x3 A2s + A4, F = x5 As + x6 A2s + x7 A4 (= Rf - x4 I);
 //                                    F^T needs A4^T, read back through a padded shared-memory transpose
-//       N  = G - I = As + (y2 + x3 x4) A2s + x4 A4 + D2      (fp32, CUDA cores)
+//       N  = G - I = As + (y2 + x3 x4) A2s + x4 A4 + Q       (fp32, CUDA cores)
 //       s squarings: N <- 2N + N N   (N^T by the same transpose)
-//   P4  D1 = R^T N^T                 A operand R^T (hi, lo) from TMEM, B = N rows
-//       R_{t+1}^T = R^T + D1         (fp32, CUDA cores; R^T kept exactly in TMEM)
+//   P4  P = R^T N^T                  A operand R^T (hi, lo) from TMEM, B = N rows
+//       R_{t+1}^T = R^T + P          (fp32, CUDA cores; R^T kept exactly in TMEM)
+// In P2 and P3 the tf32 high parts of X sit in TMEM (the columns of P, free
+// between the readout of one composition and the issue of the next), so two of
+// the three passes read only the B tile from shared memory.
 // Keeping the identity out of every tensor-core product makes the MMA's own
 // accumulation rounding scale with the small delta (|N| ~ |A|), not with |G R|.
 // The running product lives in TMEM as R^T split exactly into tf32 hi and the
 // fp32 remainder lo (R^T = hi + lo), the A operand the next composition needs.
 // The generator and q, k, v of the next position arrive by 1-D bulk TMA copies
-// into a double-buffered stage; the next position's A-build and its P1 run
-// while the current composition P4 and its readout complete (two commit
-// barriers, alternating TMEM roles).
+// into a double-buffered stage.  Operands are handed to the MMA warp one
+// 8-column chunk at a time (an mbarrier per chunk), so a product starts on its
+// first K-steps while later ones are still being written.
 #include <utility>
 
 #include "hoa_sm100.cuh"
@@ -118,6 +122,27 @@ HOA_DEVICE void put_row8(uint8_t* hi_buf, uint8_t* lo_buf, int row, int c0, cons
   }
 }
 
+// Split 8 values of row `row`, columns [c0, c0+8): the tf32 high parts are
+// returned in hi (for TMEM), the fp32 remainders lo = x - hi go to the
+// swizzled operand buffer lo_buf.
+template <int DP>
+HOA_DEVICE void split_row8(uint8_t* lo_buf, int row, int c0, const float (&v)[8], float (&hi)[8]) {
+  using L = LtLayout<DP>;
+  const int slab = c0 >> 5;
+  const int ch0 = (c0 & 31) >> 2;
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    float l[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      hi[4 * q + i] = to_tf32(v[4 * q + i]);
+      l[i] = v[4 * q + i] - hi[4 * q + i];
+    }
+    const uint32_t off = slab * L::kSlab + sw128_offset(row, ch0 + q);
+    *reinterpret_cast<float4*>(lo_buf + off) = make_float4(l[0], l[1], l[2], l[3]);
+  }
+}
+
 // One 8-column chunk j of every column group (K-steps q * NCH + j) of a 3-pass
 // SS product D = X Y, X given as rows and Y as the rows of Y^T (both K-major,
 // 128B-swizzled).  Chunk 0 (q = 0, first pass) starts the accumulation.  The
@@ -153,6 +178,23 @@ HOA_DEVICE void issue_ts_chunk(uint32_t d_tmem, uint32_t ahi, uint32_t alo, uint
     mma_tf32_ts(d_tmem, ahi + kk * 8, bhi + off, id, (J | q) ? 1u : 0u);
     mma_tf32_ts(d_tmem, ahi + kk * 8, blo + off, id, 1u);
     mma_tf32_ts(d_tmem, alo + kk * 8, bhi + off, id, 1u);
+  }
+}
+
+// The same for a 3-pass product whose A operand is split between TMEM (tf32
+// high parts, two TS passes) and shared memory (remainders, one SS pass).
+template <int DP, int J>
+HOA_DEVICE void issue_mixed_chunk(uint32_t d_tmem, uint32_t ahi, uint64_t xlo, uint64_t yhi, uint64_t ylo) {
+  using L = LtLayout<DP>;
+  constexpr uint32_t id = make_idesc(kFmtTF32, 128, DP);
+#pragma unroll
+  for (int q = 0; q < L::CQ; ++q) {
+    constexpr int kNch = L::NCH;
+    const int kk = q * kNch + J;
+    const uint64_t off = (uint64_t)(((kk >> 2) * L::kSlab + (kk & 3) * 32) >> 4);
+    mma_tf32_ts(d_tmem, ahi + kk * 8, yhi + off, id, (J | q) ? 1u : 0u);
+    mma_tf32_ts(d_tmem, ahi + kk * 8, ylo + off, id, 1u);
+    mma_tf32(d_tmem, xlo + off, yhi + off, id, 1u);
   }
 }
 
@@ -297,6 +339,7 @@ __global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, 1) link_tc_kernel(Link
       auto ss_xx = [&](auto jc) { issue_ss_chunk<DP, decltype(jc)::value>(cQ, dXhi, dXlo, dXhi, dXlo); };
       auto ss_xy = [&](auto jc) { issue_ss_chunk<DP, decltype(jc)::value>(cQ, dXhi, dXlo, dYhi, dYlo); };
       auto ts_ry = [&](auto jc) { issue_ts_chunk<DP, decltype(jc)::value>(cP, cRhi, cRlo, dYhi, dYlo); };
+      auto mx_py = [&](auto jc) { issue_mixed_chunk<DP, decltype(jc)::value>(cQ, cP, dXlo, dYhi, dYlo); };
       bool ok = product(ops_p1, ph_p1, ss_xx);                               // Q = A A^T = -A^2
       if (ok) tc_commit(done_p1);
       for (int t = t0; t < t1 && ok; ++t) {
@@ -304,11 +347,13 @@ __global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, 1) link_tc_kernel(Link
         int nsq = 0;
         ok = product(ops_main, ph_main, [&](auto jc) {
           if constexpr (decltype(jc)::value == 0) nsq = *s_nsq;
-          ss_xy(jc);
+          mx_py(jc);
         });
         if (!ok) break;
         tc_commit(done_mma);
-        for (int sq = -1; sq < nsq && ok; ++sq) {                        // Q = L F, then Q = N N
+        ok = product(ops_main, ph_main, mx_py);                           // Q = L F
+        if (ok) tc_commit(done_mma);
+        for (int sq = 0; sq < nsq && ok; ++sq) {                         // Q = N N
           ok = product(ops_main, ph_main, ss_xy);
           if (ok) tc_commit(done_mma);
         }
@@ -468,10 +513,16 @@ __global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, 1) link_tc_kernel(Link
             a2s[j][i] *= sa2;
             t1v[i] = x2 * a2s[j][i] - x1 * (av[j][i] * sa);
           }
+          float hv[8];
           if (row_ok) {
-            put_row8<DP>(Xhi, Xlo, r, c0 + 8 * j, a2s[j]);
+            split_row8<DP>(Xlo, r, c0 + 8 * j, a2s[j], hv);
             put_row8<DP>(Yhi, Ylo, r, c0 + 8 * j, t1v);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) hv[i] = 0.f;
           }
+          tmem_st8(cP + lane + c0 + 8 * j, hv);             // A2s high parts: the TS operand
+          tmem_wait_st();
           hand_over(&ops_main[j], lid);
         }
       }
@@ -546,7 +597,7 @@ __global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, 1) link_tc_kernel(Link
       {
 #pragma unroll
         for (int j = 0; j < NCH; ++j) {
-          float av[8], n0[8];
+          float av[8], n0[8], hv[8];
           tmem_ld8(cA + lane + c0 + 8 * j, av);
           tmem_wait_ld();
           if (row_ok) {
@@ -561,13 +612,15 @@ __global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, 1) link_tc_kernel(Link
               fv[i] = x6 * a2s[j][i] + x7 * a4t - x5 * as;
               n0[i] = as + c2 * a2s[j][i] + x4 * a4;
             }
-            put_row8<DP>(Xhi, Xlo, r, c0 + 8 * j, lv);
+            split_row8<DP>(Xlo, r, c0 + 8 * j, lv, hv);
             put_row8<DP>(Yhi, Ylo, r, c0 + 8 * j, fv);
           } else {
 #pragma unroll
-            for (int i = 0; i < 8; ++i) n0[i] = 0.f;
+            for (int i = 0; i < 8; ++i) { n0[i] = 0.f; hv[i] = 0.f; }
           }
           tmem_st8(cA + lane + c0 + 8 * j, n0);
+          tmem_st8(cP + lane + c0 + 8 * j, hv);             // L high parts: the TS operand
+          tmem_wait_st();
           hand_over(&ops_main[j], lid);
         }
         tmem_wait_st();

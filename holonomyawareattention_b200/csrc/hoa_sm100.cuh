@@ -189,6 +189,18 @@ HOA_DEVICE void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, ui
       : "memory");
 }
 
+// D(tmem) (+)= A(tmem) * B(smem); bf16 operands (kind::f16), fp32 accumulate.
+// A in TMEM holds two consecutive K elements per 32-bit column.
+HOA_DEVICE void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Instruction descriptor (kind::f16 / kind::tf32): fp32 accumulator, K-major A and B.
 //   bits 4-5 D format (1 = f32), 7-9 A format, 10-12 B format (1 = bf16, 2 = tf32),
 //   15/16 A/B major (0 = K), 17-22 N >> 3, 24-28 M >> 4.
