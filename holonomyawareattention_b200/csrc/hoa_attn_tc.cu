@@ -206,19 +206,25 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
     for (int j = 0; j < ni; ++j) {
       bad |= !mbar_wait_abortable(&s_full[i], j & 1, s_abort);
       tc_fence_after();
+      const int k0 = j * 128;
+      const bool diag = k0 + 127 > qi || k0 + 127 >= Tk;          // some key of the tile masked
       float sv[4][32];
 #pragma unroll
       for (int q4 = 0; q4 < 4; ++q4) tmem_ld32(cS + 32 * q4, sv[q4]);
       tmem_wait_ld();
-      const int k0 = j * 128;
-      const bool diag = k0 + 127 > qi || k0 + 127 >= Tk;          // some key of the tile masked
-      float mt = -INFINITY;
 #pragma unroll
-      for (int k = 0; k < 128; ++k) {
-        const bool ok = !diag || (k0 + k <= qi && k0 + k < Tk);
-        if (!ok) sv[k >> 5][k & 31] = -INFINITY;
-        mt = fmaxf(mt, sv[k >> 5][k & 31]);
+      for (int q4 = 0; q4 < 4; ++q4) tmem_touch(sv[q4]);
+      if (diag) {
+#pragma unroll
+        for (int k = 0; k < 128; ++k)
+          if (k0 + k > qi || k0 + k >= Tk) sv[k >> 5][k & 31] = -INFINITY;
       }
+      float mx[4];                                   // 4 independent partial maxima
+#pragma unroll
+      for (int u = 0; u < 4; ++u) mx[u] = sv[0][u];
+#pragma unroll
+      for (int k = 4; k < 128; ++k) mx[k & 3] = fmaxf(mx[k & 3], sv[k >> 5][k & 31]);
+      const float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
       const float m_cand = mt * c;
       const bool move = m_cand > m_ref + (float)kFaRescaleLog2;    // also the first tile (m_ref = -inf)
       const float m_new = move ? m_cand : m_ref;
@@ -232,6 +238,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
           float ov[16];
           tmem_ld16(cO + 16 * c16, ov);
           tmem_wait_ld();
+          tmem_touch(ov);
 #pragma unroll
           for (int e = 0; e < 16; ++e) ov[e] *= corr;
           tmem_st16(cO + 16 * c16, ov);
@@ -239,7 +246,9 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
       }
       l_run *= corr;
       m_ref = m_new;
-      float rs = 0.f;
+      // P = exp2(s c - m) as bf16 pairs over the first 64 columns of S (all of S is
+      // in registers already)
+      float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};   // 8 independent partial sums
 #pragma unroll
       for (int h = 0; h < 4; ++h) {                  // 32 keys -> 16 packed columns
         float pk[16];
@@ -247,12 +256,13 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
         for (int e = 0; e < 16; ++e) {
           const float p0 = exp2f(fmaf(sv[h][2 * e], c, -m_ref));
           const float p1 = exp2f(fmaf(sv[h][2 * e + 1], c, -m_ref));
-          rs += p0 + p1;
+          ps[(2 * e) & 7] += p0;
+          ps[(2 * e + 1) & 7] += p1;
           pk[e] = __uint_as_float(pack_bf16x2(p0, p1));
         }
         tmem_st16(cS + 16 * h, pk);
       }
-      l_run += rs;
+      l_run += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
@@ -270,6 +280,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
         float ov[16];
         tmem_ld16(cO + 16 * c16, ov);
         tmem_wait_ld();
+        tmem_touch(ov);
         if (lrow < p.Tq && !bad) {
 #pragma unroll
           for (int e = 0; e < 16; ++e)

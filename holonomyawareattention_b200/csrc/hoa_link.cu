@@ -373,7 +373,7 @@ carry_scan_kernel(const float* __restrict__ M, const float* __restrict__ carry_i
 // product: rows = 32 positions x (q, k, v), register-tiled 6 x TN per thread.
 constexpr int kApplyPos = 32;
 constexpr int kApplyRows = 3 * kApplyPos;                 // 96
-constexpr int kApplyLd = kApplyRows + 4;                  // row stride of the transposed U tile
+constexpr int kApplyLd = kApplyRows + 1;                  // row stride of the transposed U tile (odd: no bank conflicts)
 
 template <int DP> struct ApplyCfg {
   static constexpr int TN = DP >= 120 ? 8 : (DP >= 96 ? 6 : (DP >= 64 ? 4 : (DP >= 48 ? 3 : (DP >= 32 ? 2 : 1))));
@@ -383,6 +383,7 @@ template <int DP> struct ApplyCfg {
   static constexpr int ACTIVE = RG * CG;
   static constexpr int NT = ((ACTIVE + 31) / 32) * 32;
   static constexpr size_t kSmem = (size_t)(DP * DP + DP * kApplyLd + DP * kApplyPos) * sizeof(float);
+  static constexpr int kLoadPer = (kApplyRows * DP + NT - 1) / NT;   // U elements per thread and tile
 };
 
 template <int DP>
@@ -407,16 +408,29 @@ carry_apply_kernel(const float* __restrict__ U, const float* __restrict__ Cin, v
     const int r = i / DP, e = i % DP;
     Cs[i] = (r < d && e < d) ? Cg[r * d + e] : 0.f;
   }
+  // the U tile of the next step is loaded into registers while this one is computed
+  float pre[Cf::kLoadPer];
+  auto load_tile = [&](int tb) {
+    const int np = min(kApplyPos, t1 - tb);
+    const float* Ug = U + ((long long)chain * T + tb) * 3 * d;
+#pragma unroll
+    for (int k = 0; k < Cf::kLoadPer; ++k) {
+      const int i = tid + k * NT;
+      const int row = i / DP, r = i % DP;           // row = pos*3 + v
+      pre[k] = (i < kApplyRows * DP && row / 3 < np && r < d) ? Ug[(long long)row * d + r] : 0.f;
+    }
+  };
+  if (t0 < t1) load_tile(t0);
   for (int tb = t0; tb < t1; tb += kApplyPos) {
     const int np = min(kApplyPos, t1 - tb);
     __syncthreads();
-    const float* Ug = U + ((long long)chain * T + tb) * 3 * d;
-    for (int i = tid; i < kApplyRows * DP; i += NT) {
-      const int row = i / DP, r = i % DP;           // row = pos*3 + v
-      const int pp = row / 3;
-      Ut[r * kApplyLd + row] = (pp < np && r < d) ? Ug[(long long)row * d + r] : 0.f;
+#pragma unroll
+    for (int k = 0; k < Cf::kLoadPer; ++k) {
+      const int i = tid + k * NT;
+      if (i < kApplyRows * DP) Ut[(i % DP) * kApplyLd + i / DP] = pre[k];
     }
     __syncthreads();
+    if (tb + kApplyPos < t1) load_tile(tb + kApplyPos);
     float acc[TR][TN];
 #pragma unroll
     for (int i = 0; i < TR; ++i)

@@ -432,6 +432,10 @@ __global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, 1) link_tc_kernel(Link
       }
       tmem_wait_st();
     };
+    auto touch_rows = [&](float (&v)[NCH][8]) {
+#pragma unroll
+      for (int j = 0; j < NCH; ++j) tmem_touch(v[j]);
+    };
     auto ld_rows = [&](uint32_t col, float (&v)[NCH][8]) {
 #pragma unroll
       for (int j = 0; j < NCH; ++j) tmem_ld8(col + lane + c0 + 8 * j, v[j]);
@@ -484,6 +488,8 @@ __global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, 1) link_tc_kernel(Link
         ld_rows(cQ, a2s);
         ld_rows(cA, av);
         tmem_wait_ld();
+        touch_rows(a2s);
+        touch_rows(av);
         float rs = 0.f;
 #pragma unroll
         for (int j = 0; j < NCH; ++j)
@@ -540,6 +546,8 @@ __global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, 1) link_tc_kernel(Link
           tmem_ld8(cRhi + lane + c0 + 8 * j, rh[0]);
           tmem_ld8(cRlo + lane + c0 + 8 * j, rl[0]);
           tmem_wait_ld();
+          tmem_touch(rh[0]);
+          tmem_touch(rl[0]);
           float qa[8], ka[8], va[8];
           load8<QB16>(qv, c0 + 8 * j, qa);
           load8<QB16>(qv, DP + c0 + 8 * j, ka);
@@ -564,6 +572,7 @@ __global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, 1) link_tc_kernel(Link
         float a4[NCH][8];
         ld_rows(cQ, a4);
         tmem_wait_ld();
+        touch_rows(a4);
         if (row_ok) {
 #pragma unroll
           for (int j = 0; j < NCH; ++j)
@@ -600,6 +609,7 @@ __global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, 1) link_tc_kernel(Link
           float av[8], n0[8], hv[8];
           tmem_ld8(cA + lane + c0 + 8 * j, av);
           tmem_wait_ld();
+          tmem_touch(av);
           if (row_ok) {
             float lv[8], fv[8];
 #pragma unroll
@@ -633,6 +643,8 @@ __global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, 1) link_tc_kernel(Link
         ld_rows(cA, n0);
         ld_rows(cQ, nv);
         tmem_wait_ld();
+        touch_rows(n0);
+        touch_rows(nv);
 #pragma unroll
         for (int j = 0; j < NCH; ++j)
 #pragma unroll
@@ -668,6 +680,7 @@ __global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, 1) link_tc_kernel(Link
             float dq[NCH][8];
             ld_rows(cQ, dq);
             tmem_wait_ld();
+            touch_rows(dq);
 #pragma unroll
             for (int j = 0; j < NCH; ++j)
 #pragma unroll
@@ -700,6 +713,9 @@ __global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, 1) link_tc_kernel(Link
           tmem_ld8(cRlo + lane + c0 + 8 * j, rl);
           tmem_ld8(cP + lane + c0 + 8 * j, dv);
           tmem_wait_ld();
+          tmem_touch(rh);
+          tmem_touch(rl);
+          tmem_touch(dv);
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             const float v = (rh[i] + rl[i]) + dv[i];

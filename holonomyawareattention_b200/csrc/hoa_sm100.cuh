@@ -290,6 +290,14 @@ HOA_DEVICE void tmem_ld8(uint32_t taddr, float (&v)[8]) {
 
 HOA_DEVICE void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// After tmem_wait_ld: registers filled by an asynchronous TMEM load are marked
+// as written here, so that no use of them can be scheduled before the wait.
+template <int N>
+HOA_DEVICE void tmem_touch(float (&v)[N]) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) asm volatile("" : "+f"(v[i]));
+}
+
 // Store 8 consecutive TMEM columns of this thread's lane (32x32b shape, x8).
 HOA_DEVICE void tmem_st8(uint32_t taddr, const float (&v)[8]) {
   asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(
