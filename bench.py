@@ -336,7 +336,7 @@ def run_ours(args):
     peaks = load_peaks()
     s_x = 2 if dtype == torch.bfloat16 else 4
     n_pos = B * H * T
-    link_bytes = n_pos * (m_dim * 4 + 3 * d * s_x)                 # a_all fp32 + q,k,v
+    link_bytes = n_pos * (m_dim * 4 + 3 * d * s_x + d * d * 4 + 3 * d * 4)   # a, q,k,v in; R, U out
     core_bytes = n_pos * (m_dim * 4 + 4 * d * s_x)                 # + o
     f_attn = 4.0 * B * H * d * T * (T + 1) / 2
     f_rot = n_pos * 4 * 2.0 * d ** 3
@@ -356,9 +356,16 @@ def run_ours(args):
     bf16_burst = peaks["bf16_tflops"]
     link_flops = f_rot
     tf32_issued = n_pos * 4 * 3 * 2.0 * 128 * d * d
+    # DRAM traffic per launch: dram__bytes_read.sum + dram__bytes_write.sum of one ncu capture of
+    # the link kernel on c3b1 (65,536 positions, d 96, bf16 q/k/v): 3.711e9 bytes, equal to its
+    # algorithmic bytes; traffic grows in proportion to the positions, so it is scaled by them.
+    traffic = args.traffic
+    if traffic is None and d == 96 and dtype == torch.bfloat16:
+        traffic = 3.711e9 * n_pos / 65536
     roofline = {"bound": "tensor", "kernel": "link_local (kernels 1+2)",
                 "achieved": link_flops / link_s / 1e12, "peak": bf16_burst, "unit": "TFLOP/s",
-                "frac": link_flops / link_s / 1e12 / bf16_burst, "traffic": args.traffic,
+                "frac": link_flops / link_s / 1e12 / bf16_burst, "traffic": traffic,
+                "traffic_unit": "bytes per launch (DRAM read + write)",
                 "peak_source": f"bf16_tflops (of {peaks['source']})",
                 "algorithmic_flops_per_launch": link_flops,
                 "note": "algorithmic = 4 fp32-accurate d^3 products per position; see roofline_tf32_pipe"}
