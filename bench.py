@@ -332,6 +332,11 @@ def run_ours(args):
         e2e_ms = max_over_ranks(f0.elapsed_time(f1) / args.steps)
         nbytes = x.numel() * x.element_size()
 
+    # our kernels per forward: link, carry scan, carry apply, attention, inverse
+    # transport, once per batch piece of the module's forward
+    rows = max(1, mod.PIECE_TOKENS // T)
+    pieces = -(-B // rows)
+
     # ---- roofline of the dominant kernel (link_local) and the BASELINE formula
     peaks = load_peaks()
     s_x = 2 if dtype == torch.bfloat16 else 4
@@ -407,7 +412,7 @@ def run_ours(args):
         "roofline": roofline, "cpu_baseline": cpu,
         "e2e": {"value": world * B * T / (e2e_ms / 1e3), "unit": "tokens/s",
                 "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes},
-        "gpu_launches": 5 * args.steps, "clocks": clk,
+        "gpu_launches": 5 * pieces * args.steps, "clocks": clk,
         "generator_precision": generator_precision_label(mod, T, dtype),
         **extra,
     }

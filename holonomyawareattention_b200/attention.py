@@ -210,10 +210,26 @@ class PathOrderedGeometricMHA(nn.Module):
             self._w2cat_key = key
         return self._w2cat
 
+    # Batch rows are independent: the forward runs over pieces of about this many
+    # tokens (whole rows).  The edge-MLP GEMM and the link kernel then alternate in
+    # shorter bursts (measured at configs[2]: 4 pieces of 4 rows are ~5% faster
+    # than one pass, the GPU spending less time at power-capped clocks), and the
+    # per-piece generators and path products take a quarter of the memory.
+    PIECE_TOKENS = 16384
+
     def forward(self, x: torch.Tensor, attn_mask: Optional[torch.Tensor] = None,
                 return_geometry: bool = False):
         self._check_supported(x, attn_mask, return_geometry)
         B, L, D = x.shape
+        rows = max(1, self.PIECE_TOKENS // L)
+        if rows >= B:
+            return self._forward_rows(x), None
+        y = torch.empty(B, L, D, dtype=x.dtype, device=x.device)
+        for b0 in range(0, B, rows):
+            y[b0:b0 + rows] = self._forward_rows(x[b0:b0 + rows])
+        return y, None
+
+    def _forward_rows(self, x: torch.Tensor) -> torch.Tensor:
         qkv = self.qkv(x)
         if not qkv.is_contiguous():
             qkv = qkv.contiguous()
@@ -221,5 +237,4 @@ class PathOrderedGeometricMHA(nn.Module):
         heads = ops.core_forward(a_all, qkv, self.h, self.edge_scale, self.scale,
                                  out_dtype=x.dtype, hat_dtype=x.dtype, chunk=self.chunk,
                                  a_bias=a_bias)
-        y = self.out(heads)
-        return y, None
+        return self.out(heads)
