@@ -387,6 +387,12 @@ def run_ours(args):
         "roofline_baseline_formula": {
             "definition": "max(F_attn / bf16 peak, (a_all fp32 + q,k,v,o) bytes / HBM BW) over the core region",
             "target_ms": baseline_roof_s * 1e3, "core_ms": core, "frac": baseline_roof_s * 1e3 / core},
+        "roofline_extended": {
+            "definition": "max(that, F_rot / (tf32 peak / 3)): fp32-accurate rotations as 3xTF32, "
+                          "tf32 peak = measured bf16 peak / 2",
+            "target_ms": max(baseline_roof_s, f_rot / (bf16_burst / 2 / 3 * 1e12)) * 1e3,
+            "core_ms": core,
+            "frac": max(baseline_roof_s, f_rot / (bf16_burst / 2 / 3 * 1e12)) * 1e3 / core},
         "roofline_fp32_rotations": {
             "definition": "F_rot = N_pos * 4 * 2 d^3 (3 expm products + 1 composition) / link_local time, "
                           "vs FFMA peak 148 SM x 128 lanes x 2 x median SM clock (nominal, not measured)",

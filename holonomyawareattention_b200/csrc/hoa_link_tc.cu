@@ -600,13 +600,15 @@ __global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, 1) link_tc_kernel(Link
         pend |= 1u << sidx;
       }
 
-      // ---- P3 operands: X = L rows, Y^T = F^T rows; N0 = As + c2 A2s + x4 A4 -> cA.
+      float n0r[NCH][8];                                  // N0, kept until N is formed
+      // ---- P3 operands: X = L rows, Y^T = F^T rows; N0 = As + c2 A2s + x4 A4 (registers).
       //      A4 comes from the scratch copy, not from Q: P3 starts overwriting Q
       //      as soon as the first chunk is handed over.
       {
 #pragma unroll
         for (int j = 0; j < NCH; ++j) {
-          float av[8], n0[8], hv[8];
+          float av[8], hv[8];
+          float (&n0)[8] = n0r[j];
           tmem_ld8(cA + lane + c0 + 8 * j, av);
           tmem_wait_ld();
           tmem_touch(av);
@@ -628,7 +630,6 @@ __global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, 1) link_tc_kernel(Link
 #pragma unroll
             for (int i = 0; i < 8; ++i) { n0[i] = 0.f; hv[i] = 0.f; }
           }
-          tmem_st8(cA + lane + c0 + 8 * j, n0);
           tmem_st8(cP + lane + c0 + 8 * j, hv);             // L high parts: the TS operand
           tmem_wait_st();
           hand_over(&ops_main[j], lid);
@@ -639,12 +640,11 @@ __global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, 1) link_tc_kernel(Link
       // ---- N = G - I = N0 + L F, then nsq squarings N <- 2N + N N; N rows -> Y
       wait_done(done_mma, ph_mma);
       {
-        float n0[NCH][8], nv[NCH][8];
-        ld_rows(cA, n0);
+        float nv[NCH][8];
         ld_rows(cQ, nv);
         tmem_wait_ld();
-        touch_rows(n0);
         touch_rows(nv);
+        const float (&n0)[NCH][8] = n0r;
 #pragma unroll
         for (int j = 0; j < NCH; ++j)
 #pragma unroll

@@ -149,6 +149,21 @@ def test_config3_slice_bf16(precision):
     assert err <= BF16_TOL
 
 
+def test_config4_slice_bf16():
+    """configs[3] shape (T=2048, d_model=2880, H=24, head_dim 120, bf16) on one batch row vs the
+    fp32 torch restatement (head_dim 120 runs the FFMA link kernel)."""
+    B, T, D, H, es = 1, 2048, 2880, 24, 0.05
+    sd, x = seeded_case(D, H, seed=0, B=B, L=T, bf16_round=True)
+    m = PathOrderedGeometricMHA(D, n_heads=H, edge_scale=es)
+    m.load_state_dict(sd)
+    m = m.to(DEV, torch.bfloat16).eval()
+    y = run(m, x.to(DEV, torch.bfloat16))
+    ref = torch_ref.module_forward(sd, x.to(DEV), H, es, torch.float32, batch_slice=1).cpu().numpy()
+    err = O.rel_l2(y, ref)
+    print(f"c4 slice bf16 rel-L2 {err:.3e}")
+    assert err <= BF16_TOL
+
+
 def test_deterministic_and_rejects():
     z = load("d96_L32")
     m = fixture_module(z)
