@@ -5,8 +5,8 @@
 // (core/attention_fast_chunked.py:172).
 //
 // HBM-bound: every position streams its own d x d product R_t (fp32) once.
-// One warp per position; each d-row is read as float4s by 8 lanes (128 B
-// contiguous per row segment) and reduced with three shuffles.
+// One warp per position; each d-row of R_t is read as float4s by 8 lanes
+// (128 B contiguous per row segment) and reduced with three shuffles.
 #include "hoa_common.cuh"
 
 namespace hoa {
@@ -53,25 +53,48 @@ HOA_DEVICE void warp_matvec(const float* __restrict__ Mat, const float* __restri
   __syncwarp();
 }
 
+// Positions per CTA: a run of consecutive positions of one chain inside one
+// chunk, so that the chunk's carry C_k is read from global memory once per
+// CTA (into shared memory, rows padded to d+1 words) instead of once per
+// position; only R_t streams from HBM.
+constexpr int kXPos = 64;
+
 __global__ void __launch_bounds__(kXWarps * 32)
 out_transport_kernel(const float* __restrict__ o, const float* __restrict__ R,
-                     const float* __restrict__ C, int chunk, int K, void* out, int out_dtype,
-                     int H, int T, int d, long long npos) {
+                     const float* __restrict__ C, int chunk, int K, int nsub, void* out, int out_dtype,
+                     int H, int T, int d) {
   extern __shared__ __align__(16) float smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float* xo = smem + warp * 2 * d;        // o_t, then R_t w
-  float* w = xo + d;                      // C_k o_t
-  const long long pos = (long long)blockIdx.x * kXWarps + warp;
-  if (pos >= npos) return;
-  const long long chain = pos / T;
-  const int t = (int)(pos % T);
+  const int ld = d + 1;
+  float* Cs = smem;                               // [d][d+1]
+  float* xo = smem + d * ld + warp * 2 * d;       // o_t, then R_t w
+  float* w = xo + d;                              // C_k o_t
+  const long long chain = blockIdx.x / ((long long)K * nsub);
+  const int rem = (int)(blockIdx.x % ((long long)K * nsub));
+  const int kc = rem / nsub, sb = rem % nsub;
+  const int t_begin = kc * chunk + sb * kXPos;
+  const int t_end = min(min(t_begin + kXPos, (kc + 1) * chunk), T);
+  if (t_begin >= t_end) return;                   // block-uniform
+  const float* Cg = C + ((long long)chain * K + kc) * d * d;
+  for (int i = threadIdx.x; i < d * d; i += blockDim.x) Cs[(i / d) * ld + i % d] = Cg[i];
+  __syncthreads();
   const int b = (int)(chain / H), h = (int)(chain % H);
-  for (int e = lane; e < d; e += 32) xo[e] = o[pos * d + e];
-  __syncwarp();
-  warp_matvec(C + ((long long)chain * K + t / chunk) * d * d, xo, w, d, lane);
-  warp_matvec(R + pos * d * d, w, xo, d, lane);
-  const long long obase = (((long long)b * T + t) * H + h) * d;
-  for (int e = lane; e < d; e += 32) store_elem(out, obase + e, out_dtype, xo[e]);
+  for (int t = t_begin + warp; t < t_end; t += kXWarps) {
+    const long long pos = chain * T + t;
+    for (int e = lane; e < d; e += 32) xo[e] = o[pos * d + e];
+    __syncwarp();
+    for (int e = lane; e < d; e += 32) {          // w = C_k o_t (rows of C_k from shared memory)
+      const float* crow = Cs + e * ld;
+      float acc = 0.f;
+      for (int f = 0; f < d; ++f) acc = fmaf(crow[f], xo[f], acc);
+      w[e] = acc;
+    }
+    __syncwarp();
+    warp_matvec(R + pos * d * d, w, xo, d, lane);
+    const long long obase = (((long long)b * T + t) * H + h) * d;
+    for (int e = lane; e < d; e += 32) store_elem(out, obase + e, out_dtype, xo[e]);
+    __syncwarp();
+  }
 }
 
 }  // namespace hoa
@@ -84,12 +107,17 @@ extern "C" int hoa_out_transport(const float* o, const float* R, const float* C,
   if (!o || !R || !C || !out || B < 1 || H < 1 || T < 1 || d < 1 || chunk < 1)
     return HOA_ERR_INVALID_ARG;
   if (out_dtype != HOA_F32 && out_dtype != HOA_BF16) return HOA_ERR_UNSUPPORTED;
-  const long long npos = (long long)B * H * T;
-  const size_t smem = (size_t)kXWarps * 2 * d * sizeof(float);
-  const long long blocks = (npos + kXWarps - 1) / kXWarps;
-  if (blocks > 0x7fffffffLL) return HOA_ERR_UNSUPPORTED;
+  const int K = ceil_div(T, chunk);
+  const int nsub = ceil_div(min(chunk, T), kXPos);
+  const long long blocks = (long long)B * H * K * nsub;
+  if (blocks > 0x7fffffffLL || d > 128) return HOA_ERR_UNSUPPORTED;
+  const size_t smem = (size_t)(d * (d + 1) + kXWarps * 2 * d) * sizeof(float);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(out_transport_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+          cudaSuccess)
+    return HOA_ERR_LAUNCH;
   out_transport_kernel<<<(unsigned)blocks, kXWarps * 32, smem, s>>>(
-      o, R, C, chunk, ceil_div(T, chunk), out, out_dtype, H, T, d, npos);
+      o, R, C, chunk, K, nsub, out, out_dtype, H, T, d);
   return launch_status();
 }
