@@ -407,11 +407,39 @@ __global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, 1) link_tc_kernel(Link
     // -U[c][r] (c < r), 0 (c = r).
     auto build_a = [&](int s) {
       const float* av = stage_gen(s);
-      for (int row = warp; row < DP - 1; row += NW) {      // a warp per row, lanes along it
+      // a warp per row, lanes along it; every load of the warp is issued before
+      // its stores (fixed trip counts, predicated), so their latencies overlap
+      constexpr int kRows = (DP - 1 + NW - 1) / NW, kSlots = (DP - 1 + 31) / 32;
+      float ev[kRows][kSlots];
+#pragma unroll
+      for (int k = 0; k < kRows; ++k) {
+        const int row = warp + k * NW;
         const int base = row * (2 * DP - row - 1) / 2 - row - 1;
-        for (int col = row + 1 + lid; col < DP; col += 32) {
-          const float bv = bias_h != nullptr ? __ldg(bias_h + base + col) : 0.f;
-          XT[row * (DP + 1) + col] = __fmul_rn(av[base + col] + bv, es);
+#pragma unroll
+        for (int u = 0; u < kSlots; ++u) {
+          const int col = row + 1 + lid + 32 * u;
+          ev[k][u] = (row < DP - 1 && col < DP) ? av[base + col] : 0.f;
+        }
+      }
+      if (bias_h != nullptr) {
+#pragma unroll
+        for (int k = 0; k < kRows; ++k) {
+          const int row = warp + k * NW;
+          const int base = row * (2 * DP - row - 1) / 2 - row - 1;
+#pragma unroll
+          for (int u = 0; u < kSlots; ++u) {
+            const int col = row + 1 + lid + 32 * u;
+            if (row < DP - 1 && col < DP) ev[k][u] += __ldg(bias_h + base + col);
+          }
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < kRows; ++k) {
+        const int row = warp + k * NW;
+#pragma unroll
+        for (int u = 0; u < kSlots; ++u) {
+          const int col = row + 1 + lid + 32 * u;
+          if (row < DP - 1 && col < DP) XT[row * (DP + 1) + col] = __fmul_rn(ev[k][u], es);
         }
       }
       named_sync(kNamed, NT);
