@@ -67,7 +67,7 @@ def test_attn_tc_large_scores():
     assert rel_l2(o.cpu().numpy(), ref.cpu().numpy()) < 1e-2
 
 
-@pytest.mark.parametrize("d", [8, 48, 96, 120])
+@pytest.mark.parametrize("d", [6, 8, 48, 96, 120])
 def test_out_transport(d):
     torch.manual_seed(d)
     B, H, T, chunk = 2, 3, 50, 16
