@@ -13,6 +13,8 @@ _PKG = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_PKG, "libhoa.so")
 
 HOA_F32, HOA_BF16 = 0, 1
+# status codes (include/hoa.h)
+HOA_OK, HOA_ERR_INVALID_ARG, HOA_ERR_UNSUPPORTED, HOA_ERR_LAUNCH, HOA_ERR_WORKSPACE, HOA_ERR_TIMEOUT = range(6)
 
 c_int, c_float, c_size_t, c_void_p = ctypes.c_int, ctypes.c_float, ctypes.c_size_t, ctypes.c_void_p
 
@@ -42,6 +44,7 @@ SIGNATURES = {
     "hoa_core_forward_noalloc": (c_int, [c_void_p, c_int, c_void_p, c_float, c_void_p, c_int, c_void_p, c_int,
                                          c_int, c_float, c_void_p, c_void_p, c_int, c_int, c_int,
                                          c_int, c_int, c_void_p]),
+    "hoa_selftest_wait": (c_int, [c_void_p, ctypes.c_longlong, c_void_p]),
 }
 
 _lock = threading.Lock()

@@ -71,13 +71,14 @@ HOA_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity) {
 // The same bounded wait, which also gives up as soon as *abort is non-zero
 // and raises *abort itself when it times out, so that every other waiter of
 // the CTA stops promptly too.
-HOA_DEVICE bool mbar_wait_abortable(uint64_t* bar, uint32_t parity, volatile int* abort) {
+HOA_DEVICE bool mbar_wait_abortable(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                    long long max_cycles = kMaxWaitCycles) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long c0 = clock64();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort != 0) return false;
-    if (clock64() - c0 > kMaxWaitCycles) {
+    if (clock64() - c0 > max_cycles) {
       *abort = 1;
       return false;
     }

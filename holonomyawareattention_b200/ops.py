@@ -201,6 +201,17 @@ def out_transport(o: torch.Tensor, R: torch.Tensor, C: torch.Tensor, chunk: int,
     return out
 
 
+def selftest_wait(max_cycles: int, device=None) -> Tuple[int, int, int, int]:
+    """Diagnostic of the bounded device-side waits (hoa_selftest_wait): returns
+    (status of the bounded wait, 1 if the second waiter left on the abort flag,
+    the second waiter's wait in units of 1024 cycles, 1 if both waits gave up)."""
+    dev = torch.device(device if device is not None else "cuda")
+    out = torch.zeros(4, dtype=torch.int32, device=dev)
+    _lib.call("hoa_selftest_wait", _ptr(out), int(max_cycles), _stream(dev))
+    r = out.cpu().tolist()
+    return r[0], r[1], r[2], r[3]
+
+
 def uses_tensor_cores(hat_dtype: torch.dtype, d: int) -> bool:
     """Same rule as the library: bf16 hats with d % 8 == 0 and d <= 128."""
     return hat_dtype == torch.bfloat16 and d % 8 == 0 and d <= 128

@@ -181,6 +181,21 @@ int hoa_core_forward_noalloc(const void* a_all, int a_dtype, const float* a_bias
                              const float* carry_in, float* total_out,
                              int B, int H, int T, int d, int chunk, void* stream);
 
+/*
+ * hoa_selftest_wait — no counterpart in the reference.  Diagnostic for the
+ * bounded device-side waits every kernel of this library uses (mbarrier waits
+ * on TMA and tensor-core completion): one CTA of two warps waits on two
+ * mbarriers that nothing arrives at.  Warp 0 waits with a bound of max_cycles
+ * SM cycles, gives up and raises the CTA's abort flag; warp 1 waits with the
+ * library's full bound (seconds) but on the abort flag as well, so it must
+ * give up as soon as warp 0 does.  Results, written to out[0..3] (device,
+ * 4 ints): out[0] = HOA_ERR_TIMEOUT when warp 0 gave up, out[1] = 1 when
+ * warp 1 left on the abort flag, out[2] = warp 1's wait in units of 1024
+ * cycles, out[3] = 1 when both waits returned false.  Nothing faults or hangs:
+ * the GPU context stays usable.  max_cycles must be in [1, 1e9].
+ */
+int hoa_selftest_wait(int* out, long long max_cycles, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
