@@ -13,6 +13,45 @@ namespace hoa {
 
 constexpr int kXWarps = 8;
 
+// y = Mat x for a compile-time d (multiple of 4): 4 rows per pass, 8 lanes per
+// row with float4 loads; the passes are unrolled in groups of 4 so that 12
+// loads per lane are in flight together (Mat streams from HBM once).
+template <int D>
+HOA_DEVICE void warp_matvec_fixed(const float* __restrict__ Mat, const float* __restrict__ x,
+                                  float* __restrict__ y, int lane) {
+  constexpr int NC = D / 4;                      // float4 chunks per row
+  constexpr int PER = (NC + 7) / 8;              // chunks per lane and row
+  const int sub = lane & 7, rsel = lane >> 3;
+#pragma unroll 4
+  for (int e0 = 0; e0 < D; e0 += 4) {
+    const int e = e0 + rsel;
+    const float4* row = reinterpret_cast<const float4*>(Mat + (long long)e * D);
+    float4 m[PER];
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      const int c = sub + 8 * k;
+      m[k] = c < NC ? __ldg(row + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    float part = 0.f;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      const int c = sub + 8 * k;
+      if (c < NC) {
+        const float* xv = x + 4 * c;
+        part = fmaf(m[k].x, xv[0], part);
+        part = fmaf(m[k].y, xv[1], part);
+        part = fmaf(m[k].z, xv[2], part);
+        part = fmaf(m[k].w, xv[3], part);
+      }
+    }
+    part += __shfl_xor_sync(0xffffffffu, part, 1);
+    part += __shfl_xor_sync(0xffffffffu, part, 2);
+    part += __shfl_xor_sync(0xffffffffu, part, 4);
+    if (sub == 0) y[e] = part;
+  }
+  __syncwarp();
+}
+
 // y[e] = sum_f Mat[e][f] x[f] for e < d.  x, y in shared memory; Mat row-major in global.
 HOA_DEVICE void warp_matvec(const float* __restrict__ Mat, const float* __restrict__ x,
                             float* __restrict__ y, int d, int lane) {
@@ -90,7 +129,9 @@ out_transport_kernel(const float* __restrict__ o, const float* __restrict__ R,
       w[e] = acc;
     }
     __syncwarp();
-    warp_matvec(R + pos * d * d, w, xo, d, lane);
+    if (d == 96) warp_matvec_fixed<96>(R + pos * d * d, w, xo, lane);
+    else if (d == 64) warp_matvec_fixed<64>(R + pos * d * d, w, xo, lane);
+    else warp_matvec(R + pos * d * d, w, xo, d, lane);
     const long long obase = (((long long)b * T + t) * H + h) * d;
     for (int e = lane; e < d; e += 32) store_elem(out, obase + e, out_dtype, xo[e]);
     __syncwarp();
