@@ -186,14 +186,16 @@ def run_reference_arm(args):
     return 0
 
 
-def config_obj(name, n):
+def config_obj(name, n, layout="zigzag"):
     B, T, D, H, dt = CONFIGS[name]
     if name in SEQ_SHARDED:
-        return {"workload": f"{name}: B={B}, T={T} split into {n} sequence shards, d_model={D}, "
+        segs = f"{2 * n} zig-zag segments" if layout == "zigzag" else f"{n} contiguous shards"
+        return {"workload": f"{name}: B={B}, T={T} split into {segs} over {n} ranks, d_model={D}, "
                             f"H={H}, head_dim={D // H}, {dt} activations, fp32 rotations, "
                             f"edge_scale {EDGE_SCALE}",
                 "global_batch": B, "seq_len": T, "d_model": D, "heads": H, "head_dim": D // H,
-                "parallelism": f"sequence-sharded x{n} (NCCL all-gather of shard totals and K/V)",
+                "parallelism": f"sequence-sharded x{n}, {layout} (NCCL all-gather of halos, segment "
+                               f"totals and K/V)",
                 "l2": "inputs and workspace (tens of GB) far exceed the 126 MB L2"}
     return {"workload": f"{name}: B={B}/GPU, T={T}, d_model={D}, H={H}, head_dim={D // H}, {dt} "
                         f"activations, fp32 rotations, edge_scale {EDGE_SCALE}",
@@ -456,9 +458,11 @@ def run_ours(args):
 
 
 def run_seq_sharded(args):
-    """one long sequence split into contiguous shards, one per rank
-    (sequence sharding: NCCL all-gather of the shard totals and of K/V).
-    Strong scaling: the total work is fixed; value = B*T / time."""
+    """one long sequence split across the ranks (sequence sharding:
+    NCCL all-gathers of the halo tokens, the segment totals and K/V), in the
+    zig-zag layout by default (rank r holds segments r and 2N-1-r of 2N, which
+    balances the causal attention).  Strong scaling: the total work is fixed;
+    value = B*T / time."""
     import socket
     import torch
     import torch.distributed as dist
@@ -490,14 +494,14 @@ def run_seq_sharded(args):
     mod = mod.to(dtype).eval()
     g = torch.Generator(device=dev).manual_seed(1000)
     x = torch.randn(B, T, D, device=dev, generator=g).to(dtype)       # same sequence on every rank
-    s0, s1 = seqshard.shard_range(T, world, rank)
-    xs = x[:, s0:s1].contiguous()
+    layout = args.seq_layout
+    xs = seqshard.shard_sequence(x, world, rank, layout).contiguous()
     del x
     stream = torch.cuda.current_stream(dev)
     clocks = ClockSampler(physical_gpu_index(local))
     with torch.inference_mode():
         for _ in range(args.warmup):
-            seqshard.sequence_sharded_forward(mod, xs)
+            seqshard.sequence_sharded_forward(mod, xs, layout=layout)
         torch.cuda.synchronize(dev)
         dist.barrier()
         torch.cuda.synchronize(dev)
@@ -505,7 +509,7 @@ def run_seq_sharded(args):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for _ in range(args.steps):
-            y = seqshard.sequence_sharded_forward(mod, xs)
+            y = seqshard.sequence_sharded_forward(mod, xs, layout=layout)
         e1.record(stream)
         torch.cuda.synchronize(dev)
         clk = clocks.stop()
@@ -522,7 +526,7 @@ def run_seq_sharded(args):
         f0.record(stream)
         for _ in range(args.steps):
             xd.copy_(xh, non_blocking=True)
-            yy = seqshard.sequence_sharded_forward(mod, xd)
+            yy = seqshard.sequence_sharded_forward(mod, xd, layout=layout)
             yh.copy_(yy, non_blocking=True)
         f1.record(stream)
         torch.cuda.synchronize(dev)
@@ -550,7 +554,7 @@ def run_seq_sharded(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16" if dtype == torch.bfloat16 else "f32",
         "data": "synthetic (x ~ N(0,1), seeded default-init weights)",
-        "config": config_obj(args.config, world),
+        "config": config_obj(args.config, world, args.seq_layout),
         "per_gpu_tokens_s": B * T / (ms / 1e3) / world,
         "roofline": {"bound": "hbm", "kernel": "whole sharded forward",
                      "achieved": core_bytes / world / (ms / 1e3) / 1e9, "peak": peaks["hbm_gbs"],
@@ -579,6 +583,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--generator-precision", default=None, choices=[None, "auto", "split", "bf16"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--seq-layout", default="zigzag", choices=["zigzag", "contiguous"],
+                    help="shard layout of the sequence-sharded configs")
     ap.add_argument("--traffic", type=float, default=None,
                     help="ncu dram bytes per link_local launch, from a capture (scaled), if known")
     args = ap.parse_args()

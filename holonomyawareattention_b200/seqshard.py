@@ -23,7 +23,7 @@ ranks (gloo).
 """
 from __future__ import annotations
 
-from typing import Callable, Optional, Tuple
+from typing import Callable, List, Optional, Tuple
 
 import torch
 import torch.distributed as dist
@@ -95,34 +95,152 @@ def gather_kv(kh: torch.Tensor, vh: torch.Tensor, S: int, v_transposed: bool, gr
     return kh_all, vt_all
 
 
-def sequence_sharded_forward(mod, x_shard: torch.Tensor, group=None) -> torch.Tensor:
-    """y for this rank's shard of the sequence: the causal forward of
+def segments_of(layout: str, world: int, rank: int) -> Tuple[List[int], int]:
+    """(this rank's segments in the order its local tensor holds them, number of segments).
+
+    "contiguous": N segments, rank r holds segment r.
+    "zigzag": 2N segments, rank r holds segments r and 2N-1-r, so that every rank
+    does the same causal attention work (early and late queries paired)."""
+    if layout == "contiguous":
+        return [rank], world
+    if layout == "zigzag":
+        return [rank, 2 * world - 1 - rank], 2 * world
+    raise ValueError("layout must be 'contiguous' or 'zigzag'")
+
+
+def shard_sequence(x: torch.Tensor, world: int, rank: int, layout: str = "contiguous") -> torch.Tensor:
+    """This rank's local tensor (B, n_local * S, D) of a whole sequence x (B, T, D)."""
+    segs, n = segments_of(layout, world, rank)
+    T = x.shape[1]
+    if T % n != 0:
+        raise ValueError(f"sequence length {T} does not split into {n} equal segments")
+    S = T // n
+    return torch.cat([x[:, s * S:(s + 1) * S] for s in segs], dim=1)
+
+
+def unshard_sequence(parts: List[torch.Tensor], layout: str = "contiguous") -> torch.Tensor:
+    """Whole-sequence tensor from every rank's local tensor (rank order)."""
+    world = len(parts)
+    _, n = segments_of(layout, world, 0)
+    S = parts[0].shape[1] // (n // world)
+    by_seg = {}
+    for r, part in enumerate(parts):
+        segs, _ = segments_of(layout, world, r)
+        for i, sg in enumerate(segs):
+            by_seg[sg] = part[:, i * S:(i + 1) * S]
+    return torch.cat([by_seg[sg] for sg in range(n)], dim=1)
+
+
+def _gather_segments(t: torch.Tensor, layout: str, group) -> torch.Tensor:
+    """All ranks' per-segment slices stacked in segment order.  ``t`` is
+    (n_local, ...) for this rank; returns (n_segments, ...)."""
+    world, _ = _world(group)
+    parts = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(parts, t.contiguous(), group=group)
+    _, n = segments_of(layout, world, 0)
+    out = [None] * n
+    for r, part in enumerate(parts):
+        segs, _ = segments_of(layout, world, r)
+        for i, sg in enumerate(segs):
+            out[sg] = part[i]
+    return torch.stack(out, dim=0)
+
+
+def segment_halos(x_local: torch.Tensor, layout: str, group=None) -> torch.Tensor:
+    """(n_local, B, 1, D): for each local segment the token that follows it (the
+    next segment's first token; the last segment takes the sequence's first
+    token, as the reference's roll wraps)."""
+    world, rank = _world(group)
+    segs, n = segments_of(layout, world, rank)
+    B, L, D = x_local.shape
+    S = L // len(segs)
+    firsts = torch.stack([x_local[:, i * S:i * S + 1] for i in range(len(segs))], dim=0)
+    table = _gather_segments(firsts, layout, group)                 # (n, B, 1, D)
+    return torch.stack([table[(sg + 1) % n] for sg in segs], dim=0)
+
+
+def segment_carries(total_local: torch.Tensor, layout: str, group=None,
+                    compose: Optional[Callable[[torch.Tensor], torch.Tensor]] = None) -> torch.Tensor:
+    """P at the start of each local segment, (n_local, BH, d, d) fp32.
+
+    ``total_local`` (n_local, BH, d, d): each local segment's product through its
+    boundary edge.  The totals of all segments are gathered in sequence order
+    and their exclusive products taken (by default with the carry-scan kernel)."""
+    world, rank = _world(group)
+    segs, n = segments_of(layout, world, rank)
+    table = _gather_segments(total_local, layout, group)            # (n, BH, d, d)
+    C = (compose or _carry_scan_compose)(table.transpose(0, 1).contiguous())   # (BH, n, d, d)
+    return torch.stack([C[:, sg] for sg in segs], dim=0).contiguous()
+
+
+def gather_kv_segments(kh: torch.Tensor, vh: torch.Tensor, S: int, v_transposed: bool, layout: str,
+                       group=None):
+    """All segments' k^ (BH, T, d) and v^ ((BH, T, d), or transposed (BH, d, vt_stride(T))),
+    from this rank's local segments kh (n_local, BH, S, d) and vh ((n_local, BH, S, d) or
+    (n_local, BH, d, S))."""
+    world, _ = _world(group)
+    _, n = segments_of(layout, world, 0)
+    T = n * S
+    k_tab = _gather_segments(kh, layout, group)                     # (n, BH, S, d)
+    kh_all = torch.cat(list(k_tab), dim=1)
+    v_tab = _gather_segments(vh, layout, group)
+    if not v_transposed:
+        return kh_all, torch.cat(list(v_tab), dim=1)
+    BH, d = kh.shape[1], kh.shape[3]
+    vt_all = torch.zeros(BH, d, ops.vt_stride(T), dtype=vh.dtype, device=vh.device)
+    vt_all[:, :, :T] = torch.cat(list(v_tab), dim=2)
+    return kh_all, vt_all
+
+
+def sequence_sharded_forward(mod, x_shard: torch.Tensor, group=None,
+                             layout: str = "contiguous") -> torch.Tensor:
+    """y for this rank's part of the sequence: the causal forward of
     PathOrderedGeometricMHA (attn_mask = tril(T)) over the whole sequence,
-    computed with the sequence split across the ranks of ``group``."""
+    computed with the sequence split across the ranks of ``group``.
+
+    ``x_shard`` is this rank's local tensor in ``layout`` (see shard_sequence);
+    the result has the same layout.  The local segments run through the link,
+    carry and transport kernels as extra batch rows; attention runs once per
+    local segment, at that segment's query offset."""
     if mod.mode != "causal" or mod.link_mode != "interaction":
         raise NotImplementedError("sequence sharding serves mode='causal', link_mode='interaction'")
     if not x_shard.is_cuda:
         raise NotImplementedError("the B200 kernels need CUDA tensors (there is no CPU path)")
     world, rank = _world(group)
-    B, S, D = x_shard.shape
+    segs, n = segments_of(layout, world, rank)
+    nl = len(segs)
+    B, L, D = x_shard.shape
+    if L % nl != 0:
+        raise ValueError("the local tensor does not hold whole segments")
+    S = L // nl
     H, d = mod.h, mod.d
     dtype = x_shard.dtype
-    x_next = next_shard_first_token(x_shard, group)
-    qkv = mod.qkv(x_shard).contiguous()
-    a, a_bias = mod._edge_generators_nobias(x_shard, x_next, seq_len=world * S)
-    chunk = mod.chunk or ops.plan_chunk(B, H, S, d, x_shard.device)
+    halos = segment_halos(x_shard, layout, group)                   # (nl, B, 1, D)
+    # local segments as batch rows: row i*B + b is segment segs[i] of batch row b
+    xs = x_shard.view(B, nl, S, D).transpose(0, 1).reshape(nl * B, S, D)
+    x_next = halos.reshape(nl * B, 1, D)
+    qkv = mod.qkv(xs).contiguous()
+    a, a_bias = mod._edge_generators_nobias(xs, x_next, seq_len=n * S)
+    chunk = mod.chunk or ops.plan_chunk(nl * B, H, S, d, x_shard.device)
     R, U, M = ops.link_local(a.contiguous(), qkv, H, mod.edge_scale, chunk, a_bias)
     del a
-    _, total = ops.carry_scan(M, want_total=True)
-    carry_in = shard_carry_in(total, group)
+    _, total = ops.carry_scan(M, want_total=True)                   # (nl*B*H, d, d)
+    BH = B * H
+    carry_in = segment_carries(total.view(nl, BH, d, d), layout, group).view(nl * BH, d, d)
     C, _ = ops.carry_scan(M, carry_in=carry_in)
     tc = ops.uses_tensor_cores(dtype, d)
     qh, kh, vh = ops.carry_apply(U, C, chunk, dtype, v_transposed=tc)
     del U
-    kh_all, vh_all = gather_kv(kh, vh, S, tc, group)
-    if tc:
-        o = ops.attn_tc_fwd(qh, kh_all, vh_all, mod.scale, q_offset=rank * S)
-    else:
-        o = ops.attn_fwd(qh, kh_all, vh_all, mod.scale, q_offset=rank * S)
-    out = ops.out_transport(o, R, C, chunk, B, H, dtype)
-    return mod.out(out)
+    kh_seg = kh.view(nl, BH, S, d)
+    vh_seg = vh[:, :, :S].reshape(nl, BH, d, S) if tc else vh.view(nl, BH, S, d)
+    kh_all, vh_all = gather_kv_segments(kh_seg, vh_seg, S, tc, layout, group)
+    o = torch.empty(nl * BH, S, d, dtype=torch.float32, device=x_shard.device)
+    for i, sg in enumerate(segs):
+        q_i = qh[i * BH:(i + 1) * BH]
+        if tc:
+            o[i * BH:(i + 1) * BH] = ops.attn_tc_fwd(q_i, kh_all, vh_all, mod.scale, q_offset=sg * S)
+        else:
+            o[i * BH:(i + 1) * BH] = ops.attn_fwd(q_i, kh_all, vh_all, mod.scale, q_offset=sg * S)
+    out = ops.out_transport(o, R, C, chunk, nl * B, H, dtype)       # (nl*B, S, D)
+    y = mod.out(out)
+    return y.view(nl, B, S, D).transpose(0, 1).reshape(B, L, D)
