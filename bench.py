@@ -153,7 +153,10 @@ def seeded_params_np(D, H, seed=0):
 
 
 def cpu_sample_len(T):
-    return min(T, 256)
+    """Positions of the CPU sample: one sequence of up to 1024 positions (about 10 s of
+    work on the GPU host's cores at the c3 width, the cost growing with T like the
+    full workload's)."""
+    return min(T, 1024)
 
 
 def run_reference_arm(args):
