@@ -72,7 +72,9 @@ def build(force: bool = False, verbose: bool = False, extra_flags=()) -> str:
     with ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as ex:
         objs = list(ex.map(compile_one, sources()))
     tmp = LIB + ".tmp"
-    cmd = [nvcc, *ARCH, "-shared", "-o", tmp, *objs, "-lcudart"]
+    cuda_lib = os.path.join(os.path.dirname(os.path.dirname(nvcc)), "lib64")
+    cmd = [nvcc, *ARCH, "-shared", "-o", tmp, *objs, "-lcudart", "-L", cuda_lib, "-lcublasLt",
+           "-Xlinker", f"-rpath={cuda_lib}"]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

@@ -45,6 +45,8 @@ SIGNATURES = {
                                          c_int, c_float, c_void_p, c_void_p, c_int, c_int, c_int,
                                          c_int, c_int, c_void_p]),
     "hoa_selftest_wait": (c_int, [c_void_p, ctypes.c_longlong, c_void_p]),
+    "hoa_edge_gemm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p,
+                              c_size_t, c_void_p]),
 }
 
 _lock = threading.Lock()

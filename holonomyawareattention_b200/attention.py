@@ -136,11 +136,10 @@ class PathOrderedGeometricMHA(nn.Module):
                                 seq_len: Optional[int] = None):
         """(a_all, bias or None) with a_all (B, L, H*m) fp32, unscaled.
 
-        In bfloat16 the MLP's output bias is folded into the second GEMM (two
-        extra K columns of ones against the bias split into bf16 high and low
-        halves), so a_all already carries it and the bias returned is None; the
-        large fp32 output is written once by the GEMM and read once by the link
-        kernel.  In float32 nn.Linear adds it.
+        In bfloat16 the second GEMM (hoa_edge_gemm, cuBLASLt) adds the MLP's fp32
+        output bias in its epilogue, so a_all already carries it and the bias
+        returned is None; the large fp32 output is written once by the GEMM and
+        read once by the link kernel.  In float32 nn.Linear adds it.
 
         ``x_next`` (B, 1, D), for a sequence shard: the token that follows the
         shard (the next shard's first token; the whole sequence's first token
@@ -165,17 +164,16 @@ class PathOrderedGeometricMHA(nn.Module):
         h = torch.addmm(lin0.bias.float(), p2, lin0.weight.t(), out_dtype=torch.float32)
         h = F.gelu(h)
         F4 = h.shape[1]
-        # GEMM operand [h_hi | h_lo | 1 1 0 0 0 0 0 0] ("bf16": [h_hi | 1 1 0 ...]):
-        # against [W2^T ; W2^T ; b_hi ; b_lo ; 0] it gives W2 h_hi + W2 h_lo + b in fp32.
+        # GEMM operand [h_hi | h_lo] ("bf16": h_hi) against [W2^T ; W2^T] (W2^T): W2 h_hi +
+        # W2 h_lo in fp32, the bias added in the GEMM's epilogue (hoa_edge_gemm, cuBLASLt)
         nk = (2 if split else 1) * F4
-        lhs = torch.empty(B * L, nk + 8, dtype=torch.bfloat16, device=x.device)
+        lhs = torch.empty(B * L, nk, dtype=torch.bfloat16, device=x.device)
         hi = lhs[:, :F4]
         hi.copy_(h)
         if split:
-            lhs[:, F4:2 * F4].copy_(h.sub_(hi))
-        lhs[:, nk:nk + 2].fill_(1.0)
-        lhs[:, nk + 2:].zero_()
-        a = torch.mm(lhs, self._stacked_w2t(split), out_dtype=torch.float32)
+            lhs[:, F4:].copy_(h.sub_(hi))
+        wt, bias = self._stacked_w2t(split)
+        a = ops.edge_gemm(lhs, wt, bias)
         return a.view(B, L, self.h * self.m_dim), None
 
     # sequences longer than this use the split generators under "auto"
@@ -191,24 +189,18 @@ class PathOrderedGeometricMHA(nn.Module):
             return L is None or L > self.AUTO_SPLIT_ABOVE
         return p == "split"
 
-    def _stacked_w2t(self, split: bool = True) -> torch.Tensor:
-        """[W2^T ; W2^T ; b_hi ; b_lo ; 0 x 6] ((8D + 8) x m*H; without the second
-        W2^T for split=False), cached until edge_mlp.2 changes."""
+    def _stacked_w2t(self, split: bool = True):
+        """([W2^T ; W2^T] (8D x m*H; W2^T alone for split=False) in bf16, the output bias in
+        fp32), cached until edge_mlp.2 changes."""
         lin2 = self.edge_mlp[2]
         w, b = lin2.weight, lin2.bias
         key = (w.data_ptr(), w._version, b.data_ptr(), b._version, w.dtype, str(w.device), split)
         if getattr(self, "_w2cat_key", None) != key:
             wt = w.t().to(torch.bfloat16)
-            bf = b.float()
-            b_hi = bf.to(torch.bfloat16)
-            b_lo = (bf - b_hi.float()).to(torch.bfloat16)
-            tail = torch.zeros(8, wt.shape[1], dtype=torch.bfloat16, device=w.device)
-            tail[0] = b_hi
-            tail[1] = b_lo
-            parts = [wt, wt, tail] if split else [wt, tail]
-            self._w2cat = torch.cat(parts, dim=0).contiguous()
+            self._w2cat = (torch.cat([wt, wt], dim=0) if split else wt).contiguous()
+            self._b2f = b.float().contiguous()
             self._w2cat_key = key
-        return self._w2cat
+        return self._w2cat, self._b2f
 
     # Batch rows are independent: the forward runs over pieces of about this many
     # tokens (whole rows).  The edge-MLP GEMM and the link kernel then alternate in

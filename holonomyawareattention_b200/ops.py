@@ -201,6 +201,44 @@ def out_transport(o: torch.Tensor, R: torch.Tensor, C: torch.Tensor, chunk: int,
     return out
 
 
+_GEMM_WS = {}
+_GEMM_WS_BYTES = 32 << 20
+
+
+def edge_gemm(hidden: torch.Tensor, wt: torch.Tensor, bias: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """hidden (M,K) bf16 @ wt (K,N) bf16 + bias (N,) fp32 -> (M,N) fp32 (hoa_edge_gemm: one
+    cuBLASLt GEMM with the bias in its epilogue)."""
+    _need_cuda(hidden, wt)
+    if hidden.dtype != torch.bfloat16 or wt.dtype != torch.bfloat16:
+        raise NotImplementedError("hoa_edge_gemm takes bf16 operands")
+    hidden = _contig(hidden, "hidden")
+    wt = _contig(wt, "wt")
+    M, K = hidden.shape
+    if wt.shape[0] != K:
+        raise ValueError(f"wt must be (K={K}, N), got {tuple(wt.shape)}")
+    N = wt.shape[1]
+    if bias is not None:
+        if bias.dtype != torch.float32 or bias.numel() != N:
+            raise ValueError("bias must be float32 with N elements")
+        bias = bias.contiguous()
+    dev = hidden.device
+    ws = _GEMM_WS.get(dev)
+    if ws is None:
+        ws = _GEMM_WS[dev] = torch.empty(_GEMM_WS_BYTES, dtype=torch.uint8, device=dev)
+    out = torch.empty(M, N, dtype=torch.float32, device=dev)
+    try:
+        _lib.call("hoa_edge_gemm", _ptr(hidden), _ptr(wt), _ptr(bias), _ptr(out), M, N, K, _ptr(ws),
+                  _GEMM_WS_BYTES, _stream(dev))
+    except _lib.HoaError as e:
+        if e.status != _lib.HOA_ERR_UNSUPPORTED:
+            raise
+        # no cuBLASLt algorithm for this shape (e.g. rows not 16-byte aligned): torch's GEMM
+        torch.mm(hidden, wt, out_dtype=torch.float32, out=out)
+        if bias is not None:
+            out += bias
+    return out
+
+
 def selftest_wait(max_cycles: int, device=None) -> Tuple[int, int, int, int]:
     """Diagnostic of the bounded device-side waits (hoa_selftest_wait): returns
     (status of the bounded wait, 1 if the second waiter left on the abort flag,

@@ -182,6 +182,17 @@ int hoa_core_forward_noalloc(const void* a_all, int a_dtype, const float* a_bias
                              int B, int H, int T, int d, int chunk, void* stream);
 
 /*
+ * hoa_edge_gemm — the second layer of the edge MLP (core/attention_fast_chunked.py:76,
+ * `edge_mlp[2]`, whose output is the a_all of hoa_core_forward) as one cuBLASLt GEMM, a plain
+ * library GEMM: out (M x N, fp32, row-major) = hidden (M x K, bf16, row-major) * wt (K x N,
+ * bf16, row-major, i.e. W^T) + bias (N floats, nullable), fp32 accumulation, the bias added in
+ * the GEMM's epilogue.  workspace: caller-owned cuBLASLt scratch (32 MiB is plenty).  The plan
+ * of each shape is made once and cached; calls are serialised inside the library.
+ */
+int hoa_edge_gemm(const void* hidden, const void* wt, const float* bias, float* out, int M, int N,
+                  int K, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * hoa_selftest_wait — no counterpart in the reference.  Diagnostic for the
  * bounded device-side waits every kernel of this library uses (mbarrier waits
  * on TMA and tensor-core completion): one CTA of two warps waits on two

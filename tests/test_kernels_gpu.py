@@ -144,3 +144,17 @@ def test_link_local_vs_oracle(d, scale):
     qhat = torch.einsum("ntfe,ntf->nte", C[:, kidx].double(), U[:, :, 0].double()).cpu().numpy()
     qref = np.einsum("ntde,ntd->nte", Pref, q)
     assert O.rel_l2(qhat, qref) < tol
+
+
+@pytest.mark.parametrize("M,N,K", [(64, 48, 32), (1000, 1128, 768), (130, 77, 24)])
+@pytest.mark.parametrize("with_bias", [True, False])
+def test_edge_gemm_matches_torch(M, N, K, with_bias):
+    """hoa_edge_gemm (cuBLASLt, bias in the epilogue) against an fp64 product of the same bf16 values."""
+    torch.manual_seed(M + N + K)
+    h = torch.randn(M, K, device=DEV).bfloat16()
+    wt = torch.randn(K, N, device=DEV).bfloat16()
+    b = torch.randn(N, device=DEV) if with_bias else None
+    out = ops.edge_gemm(h, wt, b)
+    ref = h.double() @ wt.double() + (b.double() if with_bias else 0.0)
+    assert out.dtype == torch.float32 and out.shape == (M, N)
+    assert rel_l2(out.cpu().numpy(), ref.cpu().numpy()) < 1e-6
