@@ -284,7 +284,7 @@ def run_ours(args):
 
         # ---- core region and per-kernel timing (events on the launching stream)
         qkv = mod.qkv(x).contiguous()
-        a_all, a_bias = mod._edge_generators_nobias(x)
+        a_all, a_bias, gen_layout = mod._edge_generators_nobias(x)
         chunk = ops.plan_chunk(B, H, T, d, dev)
         torch.cuda.empty_cache()
         tc = ops.uses_tensor_cores(dtype, d)
@@ -295,7 +295,7 @@ def run_ours(args):
         for it in range(args.warmup + args.steps):
             ev = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
             ev[0].record(stream)
-            R, U, M = ops.link_local(a_all, qkv, H, EDGE_SCALE, chunk, a_bias)
+            R, U, M = ops.link_local(a_all, qkv, H, EDGE_SCALE, chunk, a_bias, gen_layout)
             ev[1].record(stream)
             C, _ = ops.carry_scan(M)
             ev[2].record(stream)

@@ -13,6 +13,7 @@ _PKG = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_PKG, "libhoa.so")
 
 HOA_F32, HOA_BF16 = 0, 1
+HOA_GEN_BANKED = 0x100        # generator layout flag OR'ed into a_dtype
 # status codes (include/hoa.h)
 HOA_OK, HOA_ERR_INVALID_ARG, HOA_ERR_UNSUPPORTED, HOA_ERR_LAUNCH, HOA_ERR_WORKSPACE, HOA_ERR_TIMEOUT = range(6)
 
@@ -24,6 +25,8 @@ SIGNATURES = {
     "hoa_max_head_dim": (c_int, []),
     "hoa_status_string": (ctypes.c_char_p, [c_int]),
     "hoa_plan_chunk": (c_int, [c_int, c_int, c_int, c_int, c_int]),
+    "hoa_gen_stride": (c_int, [c_int, c_int]),
+    "hoa_gen_banked_map": (c_int, [c_int, c_void_p]),
     "hoa_core_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int, c_int]),
     "hoa_core_forward": (c_int, [c_void_p, c_int, c_void_p, c_float, c_void_p, c_int, c_void_p, c_int, c_int,
                                  c_float, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,

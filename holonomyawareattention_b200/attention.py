@@ -124,17 +124,41 @@ class PathOrderedGeometricMHA(nn.Module):
         return ok
 
     def edge_generators(self, x: torch.Tensor) -> torch.Tensor:
-        """a_all (B, L, H*m) in fp32, unscaled: edge_mlp([x_t, x_{t+1 mod L}]).
+        """a_all (B, L, H*m) in fp32, unscaled: edge_mlp([x_t, x_{t+1 mod L}]), in the
+        reference's packed order.
 
         core/attention_fast_chunked.py:73-76 (the edge_scale multiply happens in
         the link kernel).
         """
-        a, bias = self._edge_generators_nobias(x)
-        return a if bias is None else a + bias
+        a, bias, layout = self._edge_generators_nobias(x)
+        if bias is not None:
+            a = a + bias
+        return ops.gen_from_banked(a, self.h, self.d) if layout == "banked" else a
+
+    def _gen_layout(self) -> str:
+        """Generator layout handed to the link kernel: "banked" where the head dim
+        allows it (d % 32 == 0), else the reference's packed upper triangle.  The
+        banked layout costs nothing here: the projection's output rows are
+        permuted once (and padded with a few zero rows), see _w2_rows."""
+        return "banked" if self.d % 32 == 0 else "packed"
+
+    def _w2_rows(self, w: torch.Tensor, b: torch.Tensor):
+        """The output projection's weight (H*m x F) and bias with rows in the
+        generator layout (zero rows at the banked layout's unused slots)."""
+        if self._gen_layout() == "packed":
+            return w, b
+        idx = ops.gen_banked_index(self.d, self.h, w.device)
+        width = self.h * ops.gen_stride(self.d, "banked")
+        wb = w.new_zeros(width, w.shape[1])
+        wb[idx] = w
+        bb = b.new_zeros(width)
+        bb[idx] = b
+        return wb, bb
 
     def _edge_generators_nobias(self, x: torch.Tensor, x_next: Optional[torch.Tensor] = None,
                                 seq_len: Optional[int] = None):
-        """(a_all, bias or None) with a_all (B, L, H*m) fp32, unscaled.
+        """(a_all, bias or None, layout) with a_all (B, L, H*width) fp32, unscaled,
+        in the generator layout ``layout`` (_gen_layout).
 
         In bfloat16 the second GEMM (hoa_edge_gemm, cuBLASLt) adds the MLP's fp32
         output bias in its epilogue, so a_all already carries it and the bias
@@ -154,8 +178,12 @@ class PathOrderedGeometricMHA(nn.Module):
             partner = torch.cat([x[:, 1:], x_next.to(x.dtype)], dim=1)
         pair = torch.cat([x, partner], dim=-1)
         lin0 = self.edge_mlp[0]
+        layout = self._gen_layout()
         if x.dtype == torch.float32:
-            return self.edge_mlp(pair), None
+            if layout == "packed":
+                return self.edge_mlp(pair), None, layout
+            w2, b2 = self._w2f32()
+            return F.linear(self.edge_mlp[1](lin0(pair)), w2, b2), None, layout
         if x.dtype != torch.bfloat16:
             raise NotImplementedError(f"dtype {x.dtype} is not supported (float32 or bfloat16)")
         split = self._split_generators(seq_len if seq_len is not None else
@@ -174,7 +202,7 @@ class PathOrderedGeometricMHA(nn.Module):
             lhs[:, F4:].copy_(h.sub_(hi))
         wt, bias = self._stacked_w2t(split)
         a = ops.edge_gemm(lhs, wt, bias)
-        return a.view(B, L, self.h * self.m_dim), None
+        return a.view(B, L, -1), None, layout
 
     # sequences longer than this use the split generators under "auto"
     AUTO_SPLIT_ABOVE = 8192
@@ -196,11 +224,23 @@ class PathOrderedGeometricMHA(nn.Module):
         w, b = lin2.weight, lin2.bias
         key = (w.data_ptr(), w._version, b.data_ptr(), b._version, w.dtype, str(w.device), split)
         if getattr(self, "_w2cat_key", None) != key:
-            wt = w.t().to(torch.bfloat16)
+            wr, br = self._w2_rows(w.detach(), b.detach())
+            wt = wr.t().to(torch.bfloat16)
             self._w2cat = (torch.cat([wt, wt], dim=0) if split else wt).contiguous()
-            self._b2f = b.float().contiguous()
+            self._b2f = br.float().contiguous()
             self._w2cat_key = key
         return self._w2cat, self._b2f
+
+    def _w2f32(self):
+        """(W2, b2) in fp32 with rows in the banked layout, cached until edge_mlp.2 changes."""
+        lin2 = self.edge_mlp[2]
+        w, b = lin2.weight, lin2.bias
+        key = (w.data_ptr(), w._version, b.data_ptr(), b._version, str(w.device))
+        if getattr(self, "_w2f_key", None) != key:
+            wr, br = self._w2_rows(w.detach().float(), b.detach().float())
+            self._w2f = (wr.contiguous(), br.contiguous())
+            self._w2f_key = key
+        return self._w2f
 
     # Batch rows are independent: the forward runs over pieces of about this many
     # tokens (whole rows).  The edge-MLP GEMM and the link kernel then alternate in
@@ -225,8 +265,8 @@ class PathOrderedGeometricMHA(nn.Module):
         qkv = self.qkv(x)
         if not qkv.is_contiguous():
             qkv = qkv.contiguous()
-        a_all, a_bias = self._edge_generators_nobias(x)
+        a_all, a_bias, layout = self._edge_generators_nobias(x)
         heads = ops.core_forward(a_all, qkv, self.h, self.edge_scale, self.scale,
                                  out_dtype=x.dtype, hat_dtype=x.dtype, chunk=self.chunk,
-                                 a_bias=a_bias)
+                                 a_bias=a_bias, gen_layout=layout)
         return self.out(heads)

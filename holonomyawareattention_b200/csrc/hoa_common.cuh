@@ -8,6 +8,7 @@
 #include "../../include/hoa.h"
 
 #define HOA_DEVICE __device__ __forceinline__
+#define HOA_HD __host__ __device__ __forceinline__
 
 namespace hoa {
 
@@ -36,6 +37,56 @@ inline int padded_dim(int d) {
   for (int p : dims)
     if (d <= p) return p;
   return 0;
+}
+
+// ---- generator layouts (HOA_GEN_BANKED) ----------------------------------
+// d = 32 nb.  The d x d skew matrix splits into nb x nb blocks of 32; entry
+// {i, j} has i in block a, j in block b, a <= b, offsets u = i mod 32 and
+// v = j mod 32.  The slots are laid out for the link kernel's reads, where a
+// warp holds 32 consecutive rows r and walks the columns c of one block:
+// * off-diagonal pair (a < b), bp its row-major index among the pairs a < b:
+//   line 32 bp + u (32 slots) holds row u's entries, entry v at position
+//   v ^ 4 (u mod 8).  The warp of the upper rows (r in block a) reads each
+//   lane's own line with 16-byte loads, 8 lanes hitting 8 distinct 16-byte bank
+//   groups; the warp of the lower rows (r in block b) reads one whole line per
+//   column (positions lane ^ const), one access per column.
+// * diagonal block: slot 32 k + s with bank s = (u + v) mod 32, 16 slots per
+//   bank (15 for even s; one unused).  Within a bank the entries are the pairs
+//   {u, s - u}; with w = (u - ceil(s/2)) mod 32 the partner has 31 - w (odd s)
+//   or 32 - w (even s), so min(w, partner) numbers the pairs (the w of u = v,
+//   excluded, is 0 or 16).
+HOA_HD int gen_banked_stride(int d) {
+  if (d <= 0 || d % 32 != 0) return 0;
+  const int nb = d / 32;
+  return 1024 * (nb * (nb - 1) / 2) + 512 * nb;
+}
+
+// slot of the two offsets u != v of one diagonal block, within that block's range
+HOA_HD int gen_banked_diag(int u, int v) {
+  const int s = (u + v) & 31, e = s & 1;
+  const int w = (u - ((s + 1) >> 1)) & 31;
+  const int kd = (w < 32 - e - w ? w : 32 - e - w) - 1 + e;
+  return kd * 32 + s;
+}
+
+HOA_HD int gen_banked_slot(int i, int j, int d) {   // i != j
+  if (i > j) { const int t = i; i = j; j = t; }
+  const int nb = d >> 5;
+  const int a = i >> 5, b = j >> 5, u = i & 31, v = j & 31;
+  if (a < b) {
+    const int bp = a * nb - a * (a + 1) / 2 + (b - a - 1);
+    return (bp * 32 + u) * 32 + (v ^ (4 * (u & 7)));
+  }
+  return ((nb * (nb - 1) / 2) * 32 + a * 16) * 32 + gen_banked_diag(u, v);
+}
+
+// a_dtype with the layout flag: the element type, and whether it is banked.
+inline int gen_elem_dtype(int a_dtype) { return a_dtype & ~HOA_GEN_BANKED; }
+inline bool gen_is_banked(int a_dtype) { return (a_dtype & HOA_GEN_BANKED) != 0; }
+// Floats per head of the generator row, or 0 for an unsupported combination.
+inline int gen_row_stride(int a_dtype, int d) {
+  if (!gen_is_banked(a_dtype)) return d * (d - 1) / 2;
+  return gen_elem_dtype(a_dtype) == HOA_F32 ? gen_banked_stride(d) : 0;
 }
 
 }  // namespace hoa

@@ -124,7 +124,8 @@ HOA_DEVICE int triu_row(int idx, int d) {
 }
 
 struct LinkArgs {
-  const void* a; int a_dtype; const float* a_bias; float edge_scale;
+  const void* a; int a_dtype; bool a_banked; int a_stride;  // element type, layout, floats per head
+  const float* a_bias; float edge_scale;
   const void* qkv; int qkv_dtype;
   float* R; float* U; float* M;
   int B, H, T, d, chunk, K;
@@ -172,12 +173,13 @@ __global__ void __launch_bounds__(LinkCfg<DP>::NT, 1) link_local_kernel(LinkArgs
       svec[i] = e < d ? load_elem(p.qkv, qbase + (long long)v * d + e, p.qkv_dtype) : 0.f;
     }
     // ---- edge t: A = skew(edge_scale * a_t) ------------------------------
-    const long long abase = (((long long)b * p.T + t) * p.H + h) * (long long)m;
+    const long long abase = (((long long)b * p.T + t) * p.H + h) * (long long)p.a_stride;
     for (int idx = tid; idx < m; idx += NT) {
       const int i = triu_row(idx, d);
       const int j = idx - i * (2 * d - i - 1) / 2 + i + 1;
-      float av = load_elem(p.a, abase + idx, p.a_dtype);
-      if (p.a_bias != nullptr) av += p.a_bias[(long long)h * m + idx];
+      const int slot = p.a_banked ? gen_banked_slot(i, j, d) : idx;
+      float av = load_elem(p.a, abase + slot, p.a_dtype);
+      if (p.a_bias != nullptr) av += p.a_bias[(long long)h * p.a_stride + slot];
       const float v = __fmul_rn(av, p.edge_scale);
       bufA[i * DP + j] = v;
       bufA[j * DP + i] = -v;
@@ -517,6 +519,20 @@ using namespace hoa;
 static bool valid_dtype(int t) { return t == HOA_F32 || t == HOA_BF16; }
 
 extern "C" int hoa_abi_version(void) { return 1; }
+
+extern "C" int hoa_gen_stride(int d, int banked) {
+  if (d < 2) return 0;
+  return banked ? gen_banked_stride(d) : d * (d - 1) / 2;
+}
+
+extern "C" int hoa_gen_banked_map(int d, int* slot_of_index) {
+  if (slot_of_index == nullptr || d < 2) return HOA_ERR_INVALID_ARG;
+  if (gen_banked_stride(d) == 0) return HOA_ERR_UNSUPPORTED;
+  int idx = 0;
+  for (int i = 0; i < d; ++i)
+    for (int j = i + 1; j < d; ++j) slot_of_index[idx++] = gen_banked_slot(i, j, d);
+  return HOA_OK;
+}
 extern "C" int hoa_max_head_dim(void) { return 120; }
 
 extern "C" const char* hoa_status_string(int st) {
@@ -563,13 +579,15 @@ static int link_local_dispatch(const void* a_all, int a_dtype, const float* a_bi
                                int H, int T, int d, int chunk, void* stream) {
   if (!a_all || !qkv || !R || !U || !M || B < 1 || H < 1 || T < 1 || d < 1 || chunk < 1)
     return HOA_ERR_INVALID_ARG;
-  if (!valid_dtype(a_dtype) || !valid_dtype(qkv_dtype)) return HOA_ERR_UNSUPPORTED;
+  if (!valid_dtype(gen_elem_dtype(a_dtype)) || !valid_dtype(qkv_dtype)) return HOA_ERR_UNSUPPORTED;
+  const int a_stride = gen_row_stride(a_dtype, d);
+  if (a_stride == 0) return HOA_ERR_UNSUPPORTED;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int tc = link_local_tc(a_all, a_dtype, a_bias, edge_scale, qkv, qkv_dtype, R, U, M, status,
                                B, H, T, d, chunk, s);
   if (tc != HOA_ERR_UNSUPPORTED) return tc;
-  LinkArgs a{a_all, a_dtype, a_bias, edge_scale, qkv, qkv_dtype, R, U, M, B, H, T, d, chunk,
-             ceil_div(T, chunk)};
+  LinkArgs a{a_all, gen_elem_dtype(a_dtype), gen_is_banked(a_dtype), a_stride, a_bias, edge_scale,
+             qkv, qkv_dtype, R, U, M, B, H, T, d, chunk, ceil_div(T, chunk)};
   switch (padded_dim(d)) {
     case 8: return launch_link_local<8>(a, s);
     case 16: return launch_link_local<16>(a, s);
@@ -676,8 +694,8 @@ extern "C" int hoa_core_forward(const void* a_all, int a_dtype, const float* a_b
                                 size_t workspace_bytes, void* stream) {
   if (!a_all || !qkv || !out || !workspace || B < 1 || H < 1 || T < 1 || d < 1 || chunk < 1)
     return HOA_ERR_INVALID_ARG;
-  if (!valid_dtype(a_dtype) || !valid_dtype(qkv_dtype) || !valid_dtype(out_dtype) ||
-      !valid_dtype(hat_dtype))
+  if (!valid_dtype(gen_elem_dtype(a_dtype)) || gen_row_stride(a_dtype, d) == 0 ||
+      !valid_dtype(qkv_dtype) || !valid_dtype(out_dtype) || !valid_dtype(hat_dtype))
     return HOA_ERR_UNSUPPORTED;
   if (padded_dim(d) == 0) return HOA_ERR_UNSUPPORTED;
   const CoreLayout L = core_layout(B, H, T, d, chunk, hat_dtype);

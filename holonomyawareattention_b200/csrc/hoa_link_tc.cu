@@ -73,8 +73,12 @@ struct LtLayout {
   static constexpr int kXend = offXlo + (NSLAB - 1) * kSlab + 128 * 128;
   static constexpr int kEnd0 = offXT + kXTbytes > kXend ? offXT + kXTbytes : kXend;
   static constexpr int offStage = (kEnd0 + 1023) / 1024 * 1024;
-  // one stage: the generator a_t (fp32) followed by q, k, v of position t (up to fp32)
-  static constexpr int kGenBytes = (DP * (DP - 1) / 2) * 4;
+  // one stage: the generator a_t (fp32) followed by q, k, v of position t (up to fp32);
+  // room for the larger (banked) generator layout where it exists
+  static constexpr int kGenPacked = DP * (DP - 1) / 2;
+  static constexpr int kGenBanked =
+      DP % 32 == 0 ? 1024 * ((DP / 32) * (DP / 32 - 1) / 2) + 512 * (DP / 32) : kGenPacked;
+  static constexpr int kGenBytes = kGenBanked * 4;
   static constexpr int kStage = (kGenBytes + 3 * DP * 4 + 127) / 128 * 128;
   static constexpr int offU = offStage + 2 * kStage;   // U partial sums [CQ][3][128]
   static constexpr int offMisc = offU + CQ * 3 * 128 * 4;
@@ -93,7 +97,7 @@ struct LtLayout {
 };
 
 struct LinkTcArgs {
-  const float* a; const float* a_bias; float edge_scale;
+  const float* a; const float* a_bias; float edge_scale;   // a: generator rows, packed or banked
   const void* qkv;
   float* R; float* U; float* M;
   int* status;
@@ -250,11 +254,12 @@ HOA_DEVICE void load8(const uint8_t* base, int i0, float (&v)[8]) {
 //   build A(t+1)                    with P4(t),
 //   R_{t+1} = R_t + P4 into TMEM    with P1(t+1),
 //   R_{t+1}, U_{t+1} to global      with P2(t+1).
-template <int DP, bool QB16>
+template <int DP, bool QB16, bool BANKED>
 __global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, 1) link_tc_kernel(LinkTcArgs p) {
   using L = LtLayout<DP>;
   constexpr int NCH = L::NCH, CW = L::CW, CQ = L::CQ, NT = L::NT, NW = L::NW;
-  constexpr int m = DP * (DP - 1) / 2;
+  static_assert(!BANKED || DP % 32 == 0, "the banked generator layout needs d % 32 == 0");
+  constexpr int m = BANKED ? L::kGenBanked : L::kGenPacked;   // floats per generator row
   constexpr int kQkvBytes = 3 * DP * (QB16 ? 2 : 4);
   constexpr uint32_t kNamed = 1;                          // named barrier of the compute warps
   extern __shared__ uint8_t smem_raw[];
@@ -385,8 +390,8 @@ __global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, 1) link_tc_kernel(Link
     auto stage_qkv = [&](int s) { return stage_base + s * L::kStage + L::kGenBytes; };
     auto fetch = [&](int s, int t) {        // thread 0: a_t and (q, k, v)_t into stage s
       const long long row = ((long long)b * p.T + t) * p.H + h;
-      mbar_arrive_expect_tx(&bar_a[s], (uint32_t)(L::kGenBytes + kQkvBytes));
-      bulk_load(stage_gen(s), p.a + row * m, L::kGenBytes, &bar_a[s]);
+      mbar_arrive_expect_tx(&bar_a[s], (uint32_t)(m * 4 + kQkvBytes));
+      bulk_load(stage_gen(s), p.a + row * m, m * 4, &bar_a[s]);
       bulk_load(stage_qkv(s), static_cast<const uint8_t*>(p.qkv) + row * (long long)kQkvBytes,
                 kQkvBytes, &bar_a[s]);
     };
@@ -405,7 +410,81 @@ __global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, 1) link_tc_kernel(Link
     // scratch, U[row][col] = a[S_row + col - row - 1] with S_row = row (2d - row - 1) / 2;
     // then every thread reads its row segment, A[r][c] = U[r][c] (c > r),
     // -U[c][r] (c < r), 0 (c = r).
+    // Banked layout: every thread reads its row segment straight from the stage,
+    // with no transpose scratch and no barrier (gen_banked_slot gives the
+    // layout).  A warp's columns lie in one block of 32, so the case (upper
+    // rows of an off-diagonal block pair, lower rows, or a diagonal block) is
+    // warp-uniform.  Same values as build_a below: A[r][c] = +-(a + bias) * es.
+    auto build_a_banked = [&](int s) {
+      const float* av = stage_gen(s);
+      constexpr int NB = DP / 32;
+      static_assert(!BANKED || (CW <= 32 && 32 % CW == 0), "a warp's columns must lie in one block of 32");
+      const int bc = c0 >> 5, cv = c0 & 31;        // column block and first column offset
+      float ev[NCH][8];
+      if (!row_ok) {
+#pragma unroll
+        for (int j = 0; j < NCH; ++j)
+#pragma unroll
+          for (int i = 0; i < 8; ++i) ev[j][i] = 0.f;
+      } else if (g < bc) {                         // upper rows: this lane's line, 16-byte loads
+        const int bp = g * NB - g * (g + 1) / 2 + (bc - g - 1);
+        const int line = (bp * 32 + lid) * 32, sw = lid & 7;
+#pragma unroll
+        for (int j = 0; j < NCH; ++j) {
+#pragma unroll
+          for (int h2 = 0; h2 < 2; ++h2) {
+            const int pos = 4 * ((((cv + 8 * j) >> 2) + h2) ^ sw);
+            const float4 x = *reinterpret_cast<const float4*>(av + line + pos);
+            float xv[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              if (bias_h != nullptr) xv[e] += __ldg(bias_h + line + pos + e);
+              ev[j][4 * h2 + e] = __fmul_rn(xv[e], es);
+            }
+          }
+        }
+      } else if (g > bc) {                         // lower rows: one line per column
+        const int bp = bc * NB - bc * (bc + 1) / 2 + (g - bc - 1);
+        const int line0 = (bp * 32 + cv) * 32;
+#pragma unroll
+        for (int j = 0; j < NCH; ++j)
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int slot = line0 + (8 * j + i) * 32 + (lid ^ (4 * i));   // (cv + 8j + i) mod 8 = i
+            float x = av[slot];
+            if (bias_h != nullptr) x += __ldg(bias_h + slot);
+            ev[j][i] = -__fmul_rn(x, es);
+          }
+      } else {                                     // diagonal block
+        const int base = ((NB * (NB - 1) / 2) * 32 + g * 16) * 32;
+#pragma unroll
+        for (int j = 0; j < NCH; ++j)
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            // branch-free: every lane loads, the lane with u = v from the block's
+            // first slot (in range; its value is discarded), so the warp's 32
+            // loads stay one access
+            const int v = cv + 8 * j + i;
+            const int slot = v == lid ? base : base + gen_banked_diag(lid, v);
+            float x = av[slot];
+            if (bias_h != nullptr) x += __ldg(bias_h + slot);
+            x = __fmul_rn(x, es);
+            ev[j][i] = (v == lid) ? 0.f : ((v < lid) ? -x : x);
+          }
+      }
+#pragma unroll
+      for (int j = 0; j < NCH; ++j) {
+        tmem_st8(cA + lane + c0 + 8 * j, ev[j]);
+        if (row_ok) put_row8<DP>(Xhi, Xlo, r, c0 + 8 * j, ev[j]);
+        hand_over(&ops_p1[j], lid);                       // P1 may start on this chunk
+      }
+      tmem_wait_st();
+    };
     auto build_a = [&](int s) {
+      if constexpr (BANKED) {
+        build_a_banked(s);
+        return;
+      }
       const float* av = stage_gen(s);
       // a warp per row, lanes along it; every load of the warp is issued before
       // its stores (fixed trip counts, predicated), so their latencies overlap
@@ -771,20 +850,31 @@ __global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, 1) link_tc_kernel(Link
   if (warp == 0) tmem_dealloc(tbase, L::kTmemCols);
 }
 
-template <int DP, bool QB16>
+template <int DP, bool QB16, bool BANKED>
 int launch_link_tc(const LinkTcArgs& a, cudaStream_t s) {
   using L = LtLayout<DP>;
-  if (cudaFuncSetAttribute(link_tc_kernel<DP, QB16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  if (cudaFuncSetAttribute(link_tc_kernel<DP, QB16, BANKED>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            L::kAlloc) != cudaSuccess)
     return HOA_ERR_LAUNCH;
   const long long units = (long long)a.B * a.H * a.K;
-  link_tc_kernel<DP, QB16><<<(unsigned)units, L::NTHREADS, L::kAlloc, s>>>(a);
+  link_tc_kernel<DP, QB16, BANKED><<<(unsigned)units, L::NTHREADS, L::kAlloc, s>>>(a);
   return launch_status();
 }
 
-template <int DP>
+template <int DP, bool BANKED>
 int launch_link_tc_dt(const LinkTcArgs& a, int qkv_dtype, cudaStream_t s) {
-  return qkv_dtype == HOA_BF16 ? launch_link_tc<DP, true>(a, s) : launch_link_tc<DP, false>(a, s);
+  return qkv_dtype == HOA_BF16 ? launch_link_tc<DP, true, BANKED>(a, s)
+                               : launch_link_tc<DP, false, BANKED>(a, s);
+}
+
+template <int DP>
+int launch_link_tc_layout(const LinkTcArgs& a, int qkv_dtype, bool banked, cudaStream_t s) {
+  if constexpr (DP % 32 == 0) {
+    if (banked) return launch_link_tc_dt<DP, true>(a, qkv_dtype, s);
+  } else {
+    if (banked) return HOA_ERR_UNSUPPORTED;
+  }
+  return launch_link_tc_dt<DP, false>(a, qkv_dtype, s);
 }
 
 // Entry used by hoa_link_local: returns HOA_ERR_UNSUPPORTED when this variant
@@ -792,16 +882,17 @@ int launch_link_tc_dt(const LinkTcArgs& a, int qkv_dtype, cudaStream_t s) {
 int link_local_tc(const void* a_all, int a_dtype, const float* a_bias, float edge_scale, const void* qkv,
                   int qkv_dtype, float* R, float* U, float* M, int* status, int B, int H, int T,
                   int d, int chunk, cudaStream_t s) {
-  if (a_dtype != HOA_F32 || (qkv_dtype != HOA_F32 && qkv_dtype != HOA_BF16) ||
+  if (gen_elem_dtype(a_dtype) != HOA_F32 || (qkv_dtype != HOA_F32 && qkv_dtype != HOA_BF16) ||
       (reinterpret_cast<uintptr_t>(a_all) & 15) != 0 || (reinterpret_cast<uintptr_t>(qkv) & 15) != 0)
     return HOA_ERR_UNSUPPORTED;
+  const bool banked = gen_is_banked(a_dtype);
   LinkTcArgs a{static_cast<const float*>(a_all), a_bias, edge_scale, qkv, R, U, M, status,
                B, H, T, chunk, ceil_div(T, chunk)};
   switch (d) {
-    case 32: return launch_link_tc_dt<32>(a, qkv_dtype, s);
-    case 48: return launch_link_tc_dt<48>(a, qkv_dtype, s);
-    case 64: return launch_link_tc_dt<64>(a, qkv_dtype, s);
-    case 96: return launch_link_tc_dt<96>(a, qkv_dtype, s);
+    case 32: return launch_link_tc_layout<32>(a, qkv_dtype, banked, s);
+    case 48: return launch_link_tc_layout<48>(a, qkv_dtype, banked, s);
+    case 64: return launch_link_tc_layout<64>(a, qkv_dtype, banked, s);
+    case 96: return launch_link_tc_layout<96>(a, qkv_dtype, banked, s);
     default: return HOA_ERR_UNSUPPORTED;
   }
 }

@@ -50,31 +50,99 @@ def plan_chunk(B: int, H: int, T: int, d: int, device=None) -> int:
     return int(_lib.load().hoa_plan_chunk(B, H, T, d, sms))
 
 
+# ---------------------------------------------------------------------------
+# generator layouts: "packed" (the reference's upper triangle, d(d-1)/2 floats
+# per head) and "banked" (HOA_GEN_BANKED: the same values permuted, and a few
+# unused slots, so that the link kernel reads rows without bank conflicts)
+# ---------------------------------------------------------------------------
+_BANKED_MAPS = {}
+
+
+def gen_stride(d: int, layout: str = "packed") -> int:
+    """Floats per head of a generator row in ``layout`` (0: not available for d)."""
+    if layout not in ("packed", "banked"):
+        raise ValueError("layout must be 'packed' or 'banked'")
+    return int(_lib.load().hoa_gen_stride(d, 1 if layout == "banked" else 0))
+
+
+def gen_banked_map(d: int) -> torch.Tensor:
+    """(d(d-1)/2,) int64 on the CPU: the banked slot of every packed (reference-order) entry."""
+    if d not in _BANKED_MAPS:
+        m = d * (d - 1) // 2
+        out = torch.empty(m, dtype=torch.int32)
+        _lib.call("hoa_gen_banked_map", d, out.data_ptr())
+        _BANKED_MAPS[d] = out.long()
+    return _BANKED_MAPS[d]
+
+
+def gen_banked_index(d: int, n_heads: int, device=None) -> torch.Tensor:
+    """(H*m,) int64: the banked position (h*stride + slot) of packed entry h*m + i."""
+    S = gen_stride(d, "banked")
+    slots = gen_banked_map(d)
+    idx = (torch.arange(n_heads).unsqueeze(1) * S + slots.unsqueeze(0)).reshape(-1)
+    return idx if device is None else idx.to(device)
+
+
+def gen_to_banked(a: torch.Tensor, n_heads: int, d: int) -> torch.Tensor:
+    """(..., H*m) packed generators -> (..., H*stride) banked (zeros at unused slots)."""
+    S = gen_stride(d, "banked")
+    out = a.new_zeros(*a.shape[:-1], n_heads * S)
+    out[..., gen_banked_index(d, n_heads, a.device)] = a
+    return out
+
+
+def gen_from_banked(a: torch.Tensor, n_heads: int, d: int) -> torch.Tensor:
+    """(..., H*stride) banked generators -> (..., H*m) packed."""
+    return a[..., gen_banked_index(d, n_heads, a.device)]
+
+
+def _gen_code(a_all: torch.Tensor, layout: str) -> int:
+    code = _dtype_code(a_all.dtype)
+    if layout == "banked":
+        if a_all.dtype != torch.float32:
+            raise NotImplementedError("banked generators are fp32")
+        code |= _lib.HOA_GEN_BANKED
+    elif layout != "packed":
+        raise ValueError("gen_layout must be 'packed' or 'banked'")
+    return code
+
+
+def _gen_width(n_heads: int, d: int, layout: str) -> int:
+    S = gen_stride(d, layout)
+    if S == 0:
+        raise NotImplementedError(f"the {layout} generator layout needs d % 32 == 0 (d = {d})")
+    return n_heads * S
+
+
 def core_forward(a_all: torch.Tensor, qkv: torch.Tensor, n_heads: int, edge_scale: float,
                  softmax_scale: Optional[float] = None, out_dtype: Optional[torch.dtype] = None,
                  hat_dtype: Optional[torch.dtype] = None, chunk: Optional[int] = None,
                  carry_in: Optional[torch.Tensor] = None,
                  total_out: Optional[torch.Tensor] = None,
-                 a_bias: Optional[torch.Tensor] = None) -> torch.Tensor:
+                 a_bias: Optional[torch.Tensor] = None,
+                 gen_layout: str = "packed") -> torch.Tensor:
     """Core region (kernels 1-4): a_all (B,T,H*m) and qkv (B,T,3D) -> heads (B,T,D).
 
     ``a_all`` is the raw edge-MLP output (edge_scale is applied in the kernel,
-    as core/attention_fast_chunked.py:77 does); ``a_bias`` (H*m, fp32) is the
-    MLP's output bias when the GEMM left it out.  ``carry_in`` / ``total_out``
-    are optional (B*H, d, d) fp32 tensors (see hoa_core_forward).
+    as core/attention_fast_chunked.py:77 does); ``a_bias`` (one generator row,
+    fp32) is the MLP's output bias when the GEMM left it out.  ``gen_layout``
+    "banked": a_all (B,T,H*stride) and a_bias in the banked layout
+    (gen_to_banked).  ``carry_in`` / ``total_out`` are optional (B*H, d, d) fp32
+    tensors (see hoa_core_forward).
     """
     _need_cuda(a_all, qkv, carry_in, total_out, a_bias)
     B, T, threeD = qkv.shape
     D = threeD // 3
     H = n_heads
     d = D // H
-    m = d * (d - 1) // 2
-    if a_all.shape != (B, T, H * m):
-        raise ValueError(f"a_all must be (B,T,H*m)=({B},{T},{H * m}), got {tuple(a_all.shape)}")
+    a_code = _gen_code(a_all, gen_layout)
+    width = _gen_width(H, d, gen_layout)
+    if a_all.shape != (B, T, width):
+        raise ValueError(f"a_all must be (B,T,{width}) for the {gen_layout} layout, got {tuple(a_all.shape)}")
     _contig(a_all, "a_all"); _contig(qkv, "qkv")
     if softmax_scale is None:
         softmax_scale = 1.0 / math.sqrt(d)
-    _check_bias(a_bias, H * m)
+    _check_bias(a_bias, width)
     out_dtype = out_dtype or qkv.dtype
     hat_dtype = hat_dtype or qkv.dtype
     if chunk is None:
@@ -87,7 +155,7 @@ def core_forward(a_all: torch.Tensor, qkv: torch.Tensor, n_heads: int, edge_scal
     ws_bytes = int(lib.hoa_core_workspace_bytes(B, H, T, d, chunk, hat_code))
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=qkv.device)
     out = torch.empty(B, T, D, dtype=out_dtype, device=qkv.device)
-    _lib.call("hoa_core_forward", _ptr(a_all), _dtype_code(a_all.dtype), _ptr(a_bias), float(edge_scale),
+    _lib.call("hoa_core_forward", _ptr(a_all), a_code, _ptr(a_bias), float(edge_scale),
               _ptr(qkv), _dtype_code(qkv.dtype), _ptr(out), _dtype_code(out_dtype), hat_code,
               float(softmax_scale), _ptr(carry_in), _ptr(total_out), B, H, T, d, int(chunk),
               _ptr(ws), ws_bytes, _stream(qkv.device))
@@ -104,7 +172,7 @@ def _check_bias(a_bias, n):
 
 
 def link_local(a_all: torch.Tensor, qkv: torch.Tensor, n_heads: int, edge_scale: float,
-               chunk: int, a_bias: Optional[torch.Tensor] = None
+               chunk: int, a_bias: Optional[torch.Tensor] = None, gen_layout: str = "packed"
                ) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
     """Kernel (1)+(2) local part -> (R (BH,T,d,d), U (BH,T,3,d), M (BH,K,d,d)), all fp32."""
     _need_cuda(a_all, qkv, a_bias)
@@ -112,13 +180,17 @@ def link_local(a_all: torch.Tensor, qkv: torch.Tensor, n_heads: int, edge_scale:
     H = n_heads
     d = threeD // 3 // H
     K = (T + chunk - 1) // chunk
+    a_code = _gen_code(a_all, gen_layout)
+    width = _gen_width(H, d, gen_layout)
+    if a_all.shape[-1] != width or a_all.numel() != B * T * width:
+        raise ValueError(f"a_all must be (B,T,{width}) for the {gen_layout} layout, got {tuple(a_all.shape)}")
     _contig(a_all, "a_all"); _contig(qkv, "qkv")
-    _check_bias(a_bias, H * d * (d - 1) // 2)
+    _check_bias(a_bias, width)
     dev = qkv.device
     R = torch.empty(B * H, T, d, d, dtype=torch.float32, device=dev)
     U = torch.empty(B * H, T, 3, d, dtype=torch.float32, device=dev)
     M = torch.empty(B * H, K, d, d, dtype=torch.float32, device=dev)
-    _lib.call("hoa_link_local", _ptr(a_all), _dtype_code(a_all.dtype), _ptr(a_bias), float(edge_scale), _ptr(qkv),
+    _lib.call("hoa_link_local", _ptr(a_all), a_code, _ptr(a_bias), float(edge_scale), _ptr(qkv),
               _dtype_code(qkv.dtype), _ptr(R), _ptr(U), _ptr(M), B, H, T, d, int(chunk),
               _stream(dev))
     return R, U, M
@@ -256,12 +328,12 @@ def uses_tensor_cores(hat_dtype: torch.dtype, d: int) -> bool:
 
 
 def core_stages(a_all, qkv, n_heads, edge_scale, softmax_scale, out_dtype, hat_dtype, chunk,
-                a_bias=None):
+                a_bias=None, gen_layout="packed"):
     """The core region as separate stage calls (same kernels as core_forward)."""
     B, T, threeD = qkv.shape
     H = n_heads
     d = threeD // 3 // H
-    R, U, M = link_local(a_all, qkv, H, edge_scale, chunk, a_bias)
+    R, U, M = link_local(a_all, qkv, H, edge_scale, chunk, a_bias, gen_layout)
     C, _ = carry_scan(M)
     tc = uses_tensor_cores(hat_dtype, d)
     qh, kh, vh = carry_apply(U, C, chunk, hat_dtype, v_transposed=tc)

@@ -220,9 +220,9 @@ def sequence_sharded_forward(mod, x_shard: torch.Tensor, group=None,
     xs = x_shard.view(B, nl, S, D).transpose(0, 1).reshape(nl * B, S, D)
     x_next = halos.reshape(nl * B, 1, D)
     qkv = mod.qkv(xs).contiguous()
-    a, a_bias = mod._edge_generators_nobias(xs, x_next, seq_len=n * S)
+    a, a_bias, gen_layout = mod._edge_generators_nobias(xs, x_next, seq_len=n * S)
     chunk = mod.chunk or ops.plan_chunk(nl * B, H, S, d, x_shard.device)
-    R, U, M = ops.link_local(a.contiguous(), qkv, H, mod.edge_scale, chunk, a_bias)
+    R, U, M = ops.link_local(a.contiguous(), qkv, H, mod.edge_scale, chunk, a_bias, gen_layout)
     del a
     _, total = ops.carry_scan(M, want_total=True)                   # (nl*B*H, d, d)
     BH = B * H

@@ -43,6 +43,20 @@ typedef enum {
 
 typedef enum { HOA_F32 = 0, HOA_BF16 = 1 } hoa_dtype;
 
+/*
+ * Generator layout flag, OR'ed into `a_dtype` (with HOA_F32 only, for head
+ * dims d % 32 == 0).  Without it the d(d-1)/2 generators of a head are packed
+ * as the reference packs them: the strict upper triangle row by row
+ * (core/utils.py skew_from_vec; entry (i, j), i < j, at i(2d-i-1)/2 + j-i-1).
+ * With it each head holds hoa_gen_stride(d, 1) floats and entry {i, j} sits at
+ * slot 32k + ((i + j) mod 32): a permutation of the same values (plus a few
+ * unused slots) chosen so that the link kernel reads each row of the skew
+ * matrix from shared memory without bank conflicts.  A caller gets this layout
+ * for free by permuting the output rows of the generator projection once
+ * (hoa_gen_banked_map).  Both layouts give bit-identical results.
+ */
+#define HOA_GEN_BANKED 0x100
+
 /* Library facts. */
 int hoa_abi_version(void);
 int hoa_max_head_dim(void);
@@ -52,6 +66,14 @@ const char* hoa_status_string(int status);
  * chunks (composed locally, then joined by hoa_carry_scan).  `num_sms` is the
  * device's SM count.  Returns a multiple of 16 in [16, T] (or T when T < 16). */
 int hoa_plan_chunk(int B, int H, int T, int d, int num_sms);
+
+/* Floats per head of the generator row: d(d-1)/2 (banked = 0) or the banked
+ * layout's size (banked = 1; 0 when d % 32 != 0). */
+int hoa_gen_stride(int d, int banked);
+
+/* slot_of_index[i] (i < d(d-1)/2, reference order) = the banked slot of
+ * reference entry i.  Returns HOA_ERR_UNSUPPORTED when d % 32 != 0. */
+int hoa_gen_banked_map(int d, int* slot_of_index);
 
 /* Bytes of scratch hoa_core_forward needs.  The first 4 bytes of the
  * workspace receive a device status word (0, or HOA_ERR_TIMEOUT when a

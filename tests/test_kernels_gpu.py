@@ -146,6 +146,54 @@ def test_link_local_vs_oracle(d, scale):
     assert O.rel_l2(qhat, qref) < tol
 
 
+def _offset_copy(t):
+    """A copy of t whose data starts 4 bytes past a 16-byte boundary (the
+    tensor-core link kernel declines it, so the SIMT kernel runs)."""
+    buf = torch.empty(t.numel() + 4, dtype=t.dtype, device=t.device)
+    v = buf[1:1 + t.numel()].view(t.shape)
+    v.copy_(t)
+    assert v.data_ptr() % 16 == 4
+    return v
+
+
+@pytest.mark.parametrize("d", [32, 64, 96])
+@pytest.mark.parametrize("qdtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("with_bias", [False, True])
+@pytest.mark.parametrize("simt", [False, True])
+def test_link_banked_equals_packed(d, qdtype, with_bias, simt):
+    """The banked generator layout (HOA_GEN_BANKED) gives bit-identical R, U, M
+    to the packed one, on the tensor-core and on the SIMT kernel.  Generator
+    entries of 0.3 make some positions take the squaring branch."""
+    torch.manual_seed(d + 7 * with_bias)
+    B, H, T, chunk = 2, 2, 37, 16
+    m = d * (d - 1) // 2
+    a = 0.3 * torch.randn(B, T, H * m, device=DEV)
+    bias = 0.1 * torch.randn(H * m, device=DEV) if with_bias else None
+    qkv = torch.randn(B, T, 3 * H * d, device=DEV).to(qdtype)
+    ab = ops.gen_to_banked(a, H, d)
+    bias_b = ops.gen_to_banked(bias, H, d) if with_bias else None
+    if simt:
+        a, ab = _offset_copy(a), _offset_copy(ab)
+    R1, U1, M1 = ops.link_local(a, qkv, H, 0.7, chunk, bias)
+    R2, U2, M2 = ops.link_local(ab, qkv, H, 0.7, chunk, bias_b, gen_layout="banked")
+    torch.cuda.synchronize()
+    assert torch.equal(R1, R2) and torch.equal(U1, U2) and torch.equal(M1, M2)
+    assert torch.isfinite(R1).all()
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_core_forward_banked_equals_packed(dtype):
+    torch.manual_seed(5)
+    B, T, H, d = 2, 70, 2, 96
+    m = d * (d - 1) // 2
+    a = 0.02 * torch.randn(B, T, H * m, device=DEV)
+    qkv = torch.randn(B, T, 3 * H * d, device=DEV).to(dtype)
+    y1 = ops.core_forward(a, qkv, H, 0.5, chunk=32)
+    y2 = ops.core_forward(ops.gen_to_banked(a, H, d), qkv, H, 0.5, chunk=32, gen_layout="banked")
+    torch.cuda.synchronize()
+    assert torch.equal(y1, y2)
+
+
 @pytest.mark.parametrize("M,N,K", [(64, 48, 32), (1000, 1128, 768), (130, 77, 24)])
 @pytest.mark.parametrize("with_bias", [True, False])
 def test_edge_gemm_matches_torch(M, N, K, with_bias):
