@@ -673,10 +673,10 @@ __global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, 1) link_tc_kernel(Link
         sU[(q * 3 + 2) * 128 + r] = u2;
       }
 
-      // ---- A4 = A2s T1 -> transpose scratch
+      // ---- A4 = A2s T1 -> transpose scratch (this thread's row stays in registers)
       wait_done(done_mma, ph_mma);
+      float a4[NCH][8];
       {
-        float a4[NCH][8];
         ld_rows(cQ, a4);
         tmem_wait_ld();
         touch_rows(a4);
@@ -709,8 +709,8 @@ __global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, 1) link_tc_kernel(Link
 
       float n0r[NCH][8];                                  // N0, kept until N is formed
       // ---- P3 operands: X = L rows, Y^T = F^T rows; N0 = As + c2 A2s + x4 A4 (registers).
-      //      A4 comes from the scratch copy, not from Q: P3 starts overwriting Q
-      //      as soon as the first chunk is handed over.
+      //      A4 comes from registers and A4^T from the scratch, not from Q: P3
+      //      starts overwriting Q as soon as the first chunk is handed over.
       {
 #pragma unroll
         for (int j = 0; j < NCH; ++j) {
@@ -725,11 +725,10 @@ __global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, 1) link_tc_kernel(Link
             for (int i = 0; i < 8; ++i) {
               const int col = c0 + 8 * j + i;
               const float as = av[i] * sa;
-              const float a4 = XT[r * (DP + 1) + col];
               const float a4t = XT[col * (DP + 1) + r];             // A4^T[r][col] = A4[col][r]
-              lv[i] = x3 * a2s[j][i] + a4;
+              lv[i] = x3 * a2s[j][i] + a4[j][i];
               fv[i] = x6 * a2s[j][i] + x7 * a4t - x5 * as;
-              n0[i] = as + c2 * a2s[j][i] + x4 * a4;
+              n0[i] = as + c2 * a2s[j][i] + x4 * a4[j][i];
             }
             split_row8<DP>(Xlo, r, c0 + 8 * j, lv, hv);
             put_row8<DP>(Yhi, Ylo, r, c0 + 8 * j, fv);
