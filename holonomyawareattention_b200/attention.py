@@ -7,10 +7,12 @@ core/attention_fast_chunked.py:37-60, 98).  The reference's experiments pick
 the module by import path (`--attn-module`, experiments/session_cherry.py:278,
 445), so `--attn-module holonomyawareattention_b200` selects this one.
 
-Supported inputs are exactly those of the reference's kernel drop-in
+Supported inputs are those of the reference's kernel drop-in
 (kernel/attention_kernel.py:193-208): mode "causal", attn_mask exactly
-tril(L), dropout inactive, CUDA input, return_geometry False.  Anything else
-raises NotImplementedError: there is no CPU or PyTorch fallback.
+tril(L), dropout inactive, CUDA input — plus return_geometry=True, which also
+returns {"C": P, "H": Hol} as core/attention_fast_chunked.py:175-177 does (P
+materialised by hoa_compose_paths).  Anything else raises
+NotImplementedError: there is no CPU or PyTorch fallback.
 
 Forward only.  The projections (qkv, edge_mlp, out) run as PyTorch GEMMs;
 everything between them — link rotations, prefix composition, transport,
@@ -96,8 +98,6 @@ class PathOrderedGeometricMHA(nn.Module):
             why = "mode must be 'causal'"
         elif self.link_mode != "interaction":
             why = "link_mode must be 'interaction'"
-        elif return_geometry:
-            why = "return_geometry=True is not supported"
         elif not x.is_cuda:
             why = "input must be a CUDA tensor"
         elif self.training and self.dropout.p != 0.0:
@@ -254,6 +254,16 @@ class PathOrderedGeometricMHA(nn.Module):
         self._check_supported(x, attn_mask, return_geometry)
         B, L, D = x.shape
         rows = max(1, self.PIECE_TOKENS // L)
+        if return_geometry:
+            # {"C": P (B,H,L,d,d), "H": Hol (B,H,d,d)} in x's dtype, as
+            # core/attention_fast_chunked.py:175-177 returns them
+            y = torch.empty(B, L, D, dtype=x.dtype, device=x.device)
+            P = torch.empty(B, self.h, L, self.d, self.d, dtype=x.dtype, device=x.device)
+            Hol = torch.empty(B, self.h, self.d, self.d, dtype=x.dtype, device=x.device)
+            for b0 in range(0, B, rows):
+                sl = slice(b0, min(B, b0 + rows))
+                y[sl], P[sl], Hol[sl] = self._forward_rows(x[sl], geometry=True)
+            return y, {"C": P, "H": Hol}
         if rows >= B:
             return self._forward_rows(x), None
         y = torch.empty(B, L, D, dtype=x.dtype, device=x.device)
@@ -261,11 +271,17 @@ class PathOrderedGeometricMHA(nn.Module):
             y[b0:b0 + rows] = self._forward_rows(x[b0:b0 + rows])
         return y, None
 
-    def _forward_rows(self, x: torch.Tensor) -> torch.Tensor:
+    def _forward_rows(self, x: torch.Tensor, geometry: bool = False):
         qkv = self.qkv(x)
         if not qkv.is_contiguous():
             qkv = qkv.contiguous()
         a_all, a_bias, layout = self._edge_generators_nobias(x)
+        if geometry:
+            B, L, _ = x.shape
+            chunk = self.chunk or ops.plan_chunk(B, self.h, L, self.d, x.device)
+            heads, P, Hol = ops.core_geometry(a_all, qkv, self.h, self.edge_scale, self.scale,
+                                              x.dtype, x.dtype, chunk, a_bias, layout)
+            return self.out(heads), P, Hol
         heads = ops.core_forward(a_all, qkv, self.h, self.edge_scale, self.scale,
                                  out_dtype=x.dtype, hat_dtype=x.dtype, chunk=self.chunk,
                                  a_bias=a_bias, gen_layout=layout)

@@ -273,6 +273,44 @@ def out_transport(o: torch.Tensor, R: torch.Tensor, C: torch.Tensor, chunk: int,
     return out
 
 
+def compose_paths(R: torch.Tensor, C: torch.Tensor, chunk: int, p_dtype: torch.dtype = torch.float32
+                  ) -> torch.Tensor:
+    """P_t = R_t C_{t/chunk} -> (BH, T, d, d) in p_dtype (the path products of return_geometry)."""
+    _need_cuda(R, C)
+    BH, T, d, _ = R.shape
+    _contig(R, "R"); _contig(C, "C")
+    if C.shape != (BH, (T + chunk - 1) // chunk, d, d):
+        raise ValueError("C must be (BH, ceil(T/chunk), d, d)")
+    P = torch.empty(BH, T, d, d, dtype=p_dtype, device=R.device)
+    _lib.call("hoa_compose_paths", _ptr(R), _ptr(C), _ptr(P), _dtype_code(p_dtype), BH, T, d,
+              int(chunk), _stream(R.device))
+    return P
+
+
+def core_geometry(a_all, qkv, n_heads, edge_scale, softmax_scale, out_dtype, hat_dtype, chunk,
+                  a_bias=None, gen_layout="packed", geo_dtype=None):
+    """The core region with the geometry kept: (heads (B,T,D), P (B,H,T,d,d), Hol (B,H,d,d)).
+
+    Same kernels as core_forward, run stage by stage so that the local products
+    R and the carries C survive: P_t = R_t C_{t/chunk} (hoa_compose_paths) and
+    Hol = the carry scan's total through the closing edge t = T-1
+    (core/attention_fast_chunked.py:95, 175-177).  P and Hol come in geo_dtype
+    (default: out_dtype), as the reference returns them in x's dtype."""
+    B, T, threeD = qkv.shape
+    H = n_heads
+    d = threeD // 3 // H
+    geo_dtype = geo_dtype or out_dtype
+    R, U, M = link_local(a_all, qkv, H, edge_scale, chunk, a_bias, gen_layout)
+    C, total = carry_scan(M, want_total=True)
+    tc = uses_tensor_cores(hat_dtype, d)
+    qh, kh, vh = carry_apply(U, C, chunk, hat_dtype, v_transposed=tc)
+    o = attn_tc_fwd(qh, kh, vh, softmax_scale) if tc else attn_fwd(qh, kh, vh, softmax_scale)
+    heads = out_transport(o, R, C, chunk, B, H, out_dtype)
+    del qh, kh, vh, o, U, M
+    P = compose_paths(R, C, chunk, geo_dtype).view(B, H, T, d, d)
+    return heads, P, total.view(B, H, d, d).to(geo_dtype)
+
+
 _GEMM_WS = {}
 _GEMM_WS_BYTES = 32 << 20
 

@@ -169,6 +169,16 @@ int hoa_attn_tc_fwd(const void* qh, const void* kh, const void* vhT, float* o, i
                     void* stream);
 
 /*
+ * The path products P_t = R_t C_{t/chunk} (B*H, T, d, d) in p_dtype, from the
+ * link kernel's R and the carry scan's C: the "C" entry of the reference's
+ * forward(..., return_geometry=True) (core/attention_fast_chunked.py:89-94,
+ * 175-177; its "H" entry, the holonomy, is hoa_carry_scan's total_out).  Not on
+ * the forward's path, which never materialises P.
+ */
+int hoa_compose_paths(const float* R, const float* C, void* P, int p_dtype, int BH, int T, int d,
+                      int chunk, void* stream);
+
+/*
  * Kernel (4): inverse transport out_t = R_t (C_{t/chunk} o_t), written to
  * out (B, T, H, d) in out_dtype — the input of the `out` projection.
  * Replaces core/attention_fast_chunked.py:171.

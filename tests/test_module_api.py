@@ -53,7 +53,8 @@ def test_unsupported_inputs_raise():
     inert = PathOrderedGeometricMHA(32, n_heads=4, mode="inert").eval()
     with torch.no_grad(), pytest.raises(NotImplementedError, match="causal"):
         inert(x, attn_mask=tril)
-    with torch.no_grad(), pytest.raises(NotImplementedError, match="geometry"):
+    # return_geometry=True is supported, but the CPU input is still refused
+    with torch.no_grad(), pytest.raises(NotImplementedError, match="CUDA"):
         m(x, attn_mask=tril, return_geometry=True)
 
 

@@ -119,6 +119,79 @@ def test_link_stage_geometry_vs_oracle():
         assert np.abs(np.swapaxes(P, -1, -2) @ P - I).max() < 1e-5
 
 
+def run_geometry(m, x):
+    with torch.no_grad():
+        y, geom = m(x, attn_mask=tril(x.shape[1]), return_geometry=True)
+    return y, geom
+
+
+@pytest.mark.parametrize("name", ["tiny_es01", "tiny_es15"])
+def test_return_geometry_vs_golden(name):
+    """forward(..., return_geometry=True): {"C": P, "H": Hol} against the reference's own
+    float64 geometry (core/attention_fast_chunked.py:175-177); y unchanged bit for bit."""
+    z = load(name)
+    m = fixture_module(z)
+    x = torch.from_numpy(z["x"]).to(DEV)
+    B, L, _ = x.shape
+    y, g = run_geometry(m, x)
+    assert set(g) == {"C", "H"}
+    assert g["C"].shape == (B, m.h, L, m.d, m.d) and g["H"].shape == (B, m.h, m.d, m.d)
+    assert g["C"].dtype == torch.float32 and g["H"].dtype == torch.float32
+    assert np.array_equal(y.cpu().numpy(), run(m, x))
+    assert O.rel_l2(g["C"].cpu().numpy(), z["P_f64"]) < 2e-6
+    assert O.rel_l2(g["H"].cpu().numpy(), z["Hol_f64"]) < 2e-6
+
+
+@pytest.mark.parametrize("name", ["c1", "d48_L40", "d96_L32", "d120_L24"])
+def test_return_geometry_samples(name):
+    """P at the fixture's sampled positions (batch row 0, every head) against the reference's
+    float64 P, at d = 48 (tensor-core link), 96 (banked generators) and 120 (SIMT link)."""
+    z = load(name)
+    m = fixture_module(z)
+    x = torch.from_numpy(z["x"]).to(DEV)
+    y, g = run_geometry(m, x)
+    ts = [int(t) for t in z["P_sample_t"]]
+    P = g["C"][0][:, ts].transpose(0, 1).cpu().numpy()
+    assert O.rel_l2(P, z["P_sample_b0"]) < FP32_TOL
+    assert np.array_equal(y.cpu().numpy(), run(m, x))
+    Pf = g["C"].double()
+    eye = torch.eye(m.d, dtype=torch.float64, device=DEV)
+    assert (Pf.transpose(-1, -2) @ Pf - eye).abs().max().item() < 1e-5
+
+
+def test_return_geometry_bf16_in_pieces():
+    """bf16 module, forward split into one-row batch pieces: P and Hol come back in bf16,
+    y equals the forward without geometry, P matches the float64 samples within the bf16 bar."""
+    z = load("bf16_d48_L64")
+    m = fixture_module(z, torch.bfloat16)
+    m.PIECE_TOKENS = int(z["L"])                       # one batch row per piece
+    x = torch.from_numpy(z["x"]).to(DEV, torch.bfloat16)
+    y, g = run_geometry(m, x)
+    assert g["C"].dtype == torch.bfloat16 and g["H"].dtype == torch.bfloat16
+    ts = [int(t) for t in z["P_sample_t"]]
+    P = g["C"][0][:, ts].transpose(0, 1).float().cpu().numpy()
+    assert O.rel_l2(P, z["P_sample_b0"]) < BF16_TOL
+    with torch.no_grad():
+        y0, _ = m(x, attn_mask=tril(x.shape[1]))
+    assert torch.equal(y, y0)
+
+
+@pytest.mark.parametrize("d,T,chunk", [(8, 37, 16), (48, 100, 32), (96, 33, 16), (120, 20, 8)])
+@pytest.mark.parametrize("p_dtype", [torch.float32, torch.bfloat16])
+def test_compose_paths_kernel(d, T, chunk, p_dtype):
+    """hoa_compose_paths: P_t = R_t C_{t/chunk} against a float64 product, ragged last chunk."""
+    torch.manual_seed(d + T)
+    BH = 3
+    K = (T + chunk - 1) // chunk
+    R = torch.randn(BH, T, d, d, device=DEV)
+    C = torch.randn(BH, K, d, d, device=DEV)
+    P = ops.compose_paths(R, C, chunk, p_dtype)
+    kidx = torch.arange(T, device=DEV) // chunk
+    ref = torch.einsum("ntij,ntjk->ntik", R.double(), C[:, kidx].double())
+    tol = 1e-6 if p_dtype == torch.float32 else 5e-3
+    assert O.rel_l2(P.double().cpu().numpy(), ref.cpu().numpy()) < tol
+
+
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_config2_full_size(dtype):
     """B=64, T=512, d_model=192, H=4 against the torch restatement (fp32)."""
