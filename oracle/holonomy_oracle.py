@@ -19,6 +19,8 @@ reference's behaviour (SiddhiMali/HolonomyAwareAttention):
 * causal softmax fold, finfo.min masking,
   l.clamp_min(1e-20), out = P o               core/attention_fast_chunked.py:119-171
 * output projection                           core/attention_fast_chunked.py:172-173
+* any mask, the wrap pairs through Hol, the
+  inert ablation, the additive link           core/attention.py:69-195 (forward_general)
 
 The reference's causal+tril result equals core/attention.py:156-195 (its O(L^3)
 arc walk); the golden fixtures under tests/golden pin both.
@@ -65,10 +67,14 @@ class Params:
     b1: np.ndarray           # (4D,)             edge_mlp.0.bias
     w2: np.ndarray           # (m*H, 4D)         edge_mlp.2.weight
     b2: np.ndarray           # (m*H,)            edge_mlp.2.bias
+    gq: Optional[np.ndarray] = None   # (m*H, D)  gqproj.weight (link_mode "additive")
+    gk: Optional[np.ndarray] = None   # (m*H, D)  gkproj.weight
 
     @staticmethod
     def from_state_dict(sd, dtype=np.float64) -> "Params":
         def g(k):
+            if k not in sd:
+                return None
             t = sd[k]
             if hasattr(t, "detach"):
                 t = t.detach().float().cpu().numpy() if str(t.dtype) == "torch.bfloat16" \
@@ -76,11 +82,12 @@ class Params:
             return np.asarray(t, dtype=dtype)
 
         return Params(g("qkv.weight"), g("out.weight"), g("edge_mlp.0.weight"),
-                      g("edge_mlp.0.bias"), g("edge_mlp.2.weight"), g("edge_mlp.2.bias"))
+                      g("edge_mlp.0.bias"), g("edge_mlp.2.weight"), g("edge_mlp.2.bias"),
+                      g("gqproj.weight"), g("gkproj.weight"))
 
     def astype(self, dtype) -> "Params":
-        return Params(*(np.asarray(a, dtype=dtype) for a in
-                        (self.qkv, self.out, self.w1, self.b1, self.w2, self.b2)))
+        return Params(*(None if a is None else np.asarray(a, dtype=dtype) for a in
+                        (self.qkv, self.out, self.w1, self.b1, self.w2, self.b2, self.gq, self.gk)))
 
 
 def round_bf16(a: np.ndarray) -> np.ndarray:
@@ -171,6 +178,17 @@ def edge_generators(p: Params, x: np.ndarray, n_heads: int, edge_scale: float) -
     return a * x.dtype.type(edge_scale)
 
 
+def edge_generators_additive(p: Params, x: np.ndarray, n_heads: int, edge_scale: float) -> np.ndarray:
+    """link_mode "additive": a_t = edge_scale * (gq(x_t) + gk(x_{t+1 mod L})), (B,H,L,m)
+    (core/attention.py:98-101: edges t < L-1 pair gq_t with gk_{t+1}, the closing
+    edge gq_{L-1} with gk_0)."""
+    B, L, D = x.shape
+    d = D // n_heads
+    m = d * (d - 1) // 2
+    a = x @ p.gq.T + np.roll(x @ p.gk.T, -1, axis=1)
+    return a.reshape(B, L, n_heads, m).transpose(0, 2, 1, 3) * x.dtype.type(edge_scale)
+
+
 def prefix_products(G_adj: np.ndarray) -> np.ndarray:
     """P_0 = I, P_{t+1} = G_t P_t (core/attention_fast_chunked.py:89-94). G_adj (...,L-1,d,d)."""
     *lead, Lm1, d, _ = G_adj.shape
@@ -227,6 +245,76 @@ def forward(p: Params, x: np.ndarray, n_heads: int, edge_scale: float,
         return y
     return y, dict(q=q, k=k, v=v, a_all=a_all, P=P, Hol=Hol, qh=qh, kh=kh, vh=vh, o=o,
                    heads=heads)
+
+
+def masked_attention(qh, kh, vh, scale, mask=None, kw=None, vw=None):
+    """softmax_j(q_i . key_ij * scale) over ALL keys, masked entries at finfo.min (so a
+    fully masked row averages uniformly, as core/attention_fast_chunked.py:142-148 does),
+    the sum divided by l.clamp_min(1e-20).  key_ij / value_ij are kh_j / vh_j for j <= i
+    and, when kw / vw are given, kw_j / vw_j for the wrap pairs j > i."""
+    L = qh.shape[-2]
+    s = (qh @ np.swapaxes(kh, -1, -2)) * scale
+    base = np.tril(np.ones((L, L), dtype=bool))
+    if kw is not None:
+        s = np.where(base, s, (qh @ np.swapaxes(kw, -1, -2)) * scale)
+    if mask is not None:
+        s = np.where(np.asarray(mask, dtype=bool), s, np.finfo(qh.dtype).min)
+    mx = s.max(axis=-1, keepdims=True)
+    pr = np.exp(s - mx)
+    l = pr.sum(axis=-1, keepdims=True)
+    if kw is None:
+        o = pr @ vh
+    else:
+        o = (pr * base) @ vh + (pr * ~base) @ vw
+    return o / np.maximum(l, 1e-20)
+
+
+def forward_general(p: Params, x: np.ndarray, n_heads: int, edge_scale: float, mask=None,
+                    mode: str = "causal", link_mode: str = "interaction", dtype=np.float64,
+                    return_intermediates: bool = False):
+    """core/attention.py:69-195 for any mask (None = all allowed), both modes and
+    both link forms, in the P / Hol form of core/attention_fast_chunked.py:98-171.
+
+    "causal" (arc transport, core/attention.py:156-165): the transport j -> i walks
+    the ring, G_arc[i][j] = P_i P_j^T for j <= i and P_i Hol P_j^T for the wrap
+    pairs j > i, so with q^ = P^T q etc. the wrap pairs see Hol k^_j and Hol v^_j.
+    (core/attention_fast_chunked.py:116-117 applies Hol^T there; under the tril
+    mask those pairs never count.)  "inert" (:166-169): G_arc[i][j] = P_i^T P_j, so
+    q~ = P q, k~ = P k, v~ = P v and out_i = P_i^T o_i."""
+    p = p.astype(dtype)
+    x = np.asarray(x, dtype=dtype)
+    B, L, D = x.shape
+    H = n_heads
+    d = D // H
+    q, k, v = project_qkv(p, x, H)
+    if link_mode == "interaction":
+        a_all = edge_generators(p, x, H, edge_scale)
+    elif link_mode == "additive":
+        a_all = edge_generators_additive(p, x, H, edge_scale)
+    else:
+        raise ValueError(link_mode)
+    G_adj = expm(skew_from_vec(a_all[:, :, :-1], d))
+    G_close = expm(skew_from_vec(a_all[:, :, -1], d))
+    P = prefix_products(G_adj)
+    Hol = G_close @ P[:, :, L - 1]
+    scale = 1.0 / math.sqrt(d)
+    if mode == "causal":
+        PT = np.swapaxes(P, -1, -2)
+        qh, kh, vh = ((PT @ t[..., None])[..., 0] for t in (q, k, v))
+        kw = (Hol[:, :, None] @ kh[..., None])[..., 0]
+        vw = (Hol[:, :, None] @ vh[..., None])[..., 0]
+        o = masked_attention(qh, kh, vh, scale, mask, kw, vw)
+        heads = (P @ o[..., None])[..., 0]
+    elif mode == "inert":
+        qh, kh, vh = ((P @ t[..., None])[..., 0] for t in (q, k, v))
+        o = masked_attention(qh, kh, vh, scale, mask)
+        heads = (np.swapaxes(P, -1, -2) @ o[..., None])[..., 0]
+    else:
+        raise ValueError(mode)
+    y = heads.transpose(0, 2, 1, 3).reshape(B, L, D) @ p.out.T
+    if not return_intermediates:
+        return y
+    return y, dict(P=P, Hol=Hol, a_all=a_all, o=o, heads=heads)
 
 
 def core_forward(a_all: np.ndarray, q: np.ndarray, k: np.ndarray, v: np.ndarray,

@@ -96,6 +96,64 @@ def case(name, core, chunk, D, H, es, seed, B, L, *, store_weights, use_orig, bf
     print(f"{name}: {time.time() - t0:.1f}s", flush=True)
 
 
+def make_mask(kind, L, seed):
+    """(L, L) bool, True = allowed: None (no mask), a seeded random mask with the
+    diagonal allowed, or a band |i - j| <= L // 4 (both wrap pairs and blocked pairs)."""
+    if kind == "none":
+        return None
+    if kind == "random":
+        g = torch.Generator().manual_seed(seed + 100)
+        m = torch.rand(L, L, generator=g) < 0.6
+        return m | torch.eye(L, dtype=torch.bool)
+    if kind == "band":
+        i = torch.arange(L)
+        return (i.view(L, 1) - i.view(1, L)).abs() <= L // 4
+    raise ValueError(kind)
+
+
+def general_case(name, core, D, H, es, seed, B, L, mask_kind, mode, link_mode):
+    """core/attention.py (the O(L^3) original: arc transport through the closing
+    edge, any mask, the inert ablation, the additive link) on seeded inputs."""
+    t0 = time.time()
+    torch.manual_seed(seed)
+    m = core.PathOrderedGeometricMHA(D, n_heads=H, edge_scale=es, mode=mode).eval()
+    m.link_mode = link_mode
+    x = torch.randn(B, L, D)
+    mask = make_mask(mask_kind, L, seed)
+    rec = dict(B=B, L=L, D=D, H=H, edge_scale=es, seed=seed, mode=mode, link_mode=link_mode,
+               mask_kind=mask_kind, x=x.numpy())
+    if mask is not None:
+        rec["mask"] = mask.numpy()
+    for dt, tag in ((torch.float32, "f32"), (torch.float64, "f64")):
+        mm = m.to(dt)
+        with torch.no_grad():
+            y, g = mm(x.to(dt), attn_mask=mask, return_geometry=True)
+        rec["y_orig_" + tag] = y.numpy()
+        if dt == torch.float64:
+            rec["Hol_f64"] = g["H"].numpy()
+            rec["P_f64"] = g["C"].numpy()
+    m.float()
+    sd = m.state_dict()
+    if D <= 32:
+        for k, v in sd.items():
+            rec["w:" + k] = v.numpy().astype(np.float32)
+    else:                                          # regenerated from the seed at test time
+        for k, v in checksums(sd).items():
+            rec["cs:" + k] = v
+    np.savez_compressed(os.path.join(HERE, name + ".npz"), **rec)
+    print(f"{name}: {time.time() - t0:.1f}s", flush=True)
+
+
+def general_cases(core):
+    # causal arc transport with the wrap pairs live (no mask, random, band), large rotations
+    general_case("gen_none_es15", core, 32, 4, 1.5, 7, 2, 12, "none", "causal", "interaction")
+    general_case("gen_rand_es15", core, 32, 4, 1.5, 8, 2, 12, "random", "causal", "interaction")
+    general_case("gen_band_d48", core, 96, 2, 0.5, 9, 1, 16, "band", "causal", "interaction")
+    # the inert ablation (endpoint transport P_i^T P_j) and the additive link
+    general_case("gen_inert_rand", core, 32, 4, 1.5, 10, 2, 12, "random", "inert", "interaction")
+    general_case("gen_additive_none", core, 32, 4, 1.5, 11, 2, 12, "none", "causal", "additive")
+
+
 def expm_case():
     rec = {}
     for d, seed in ((8, 10), (48, 11), (96, 12), (120, 13)):
@@ -115,12 +173,17 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True, help="reference checkout (folder holding core/)")
     ap.add_argument("--skip-c1", action="store_true")
+    ap.add_argument("--only-general", action="store_true",
+                    help="write only the core/attention.py cases (masks, wrap, inert, additive)")
     args = ap.parse_args()
     sys.path.insert(0, os.path.join(args.ref, "core"))
     torch.set_num_threads(os.cpu_count())
     import attention as core                      # core/attention.py
     import attention_fast_chunked as chunk        # core/attention_fast_chunked.py
 
+    general_cases(core)
+    if args.only_general:
+        return
     expm_case()
     # the reference self-test shape (core/attention_fast_chunked.py:214-236), default edge_scale
     case("tiny_es01", core, chunk, 32, 4, 0.1, 0, 2, 12, store_weights=True, use_orig=True)

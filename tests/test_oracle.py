@@ -114,3 +114,55 @@ def test_round_bf16():
     r = O.round_bf16(v)
     t = torch.from_numpy(v).to(torch.bfloat16).float().numpy()
     np.testing.assert_array_equal(r, t)
+
+
+GENERAL = ["gen_none_es15", "gen_rand_es15", "gen_band_d48", "gen_inert_rand", "gen_additive_none"]
+
+
+def general_case(name):
+    """(params, x, mask, fixture) of a core/attention.py case (masks, wrap, inert, additive)."""
+    z = np.load(os.path.join(GOLD, name + ".npz"))
+    D, H, seed, B, L = (int(z[k]) for k in ("D", "H", "seed", "B", "L"))
+    if "w:qkv.weight" in z.files:
+        sd = {k[2:]: torch.from_numpy(z[k]) for k in z.files if k.startswith("w:")}
+    else:
+        sd, _ = seeded_case(D, H, seed, B, L)
+        cs = checksums(sd)
+        for k in cs:
+            assert np.allclose(cs[k], z["cs:" + k]), k
+    mask = z["mask"] if "mask" in z.files else None
+    return params_of(sd), z["x"], mask, z
+
+
+@pytest.mark.parametrize("name", GENERAL)
+def test_forward_general_vs_original(name):
+    """forward_general against core/attention.py itself (the O(L^3) arc walk) in float64:
+    any mask, wrap pairs through the closing edge, the inert ablation, the additive link."""
+    p, x, mask, z = general_case(name)
+    y, inter = O.forward_general(p, x, int(z["H"]), float(z["edge_scale"]), mask, str(z["mode"]),
+                                 str(z["link_mode"]), np.float64, return_intermediates=True)
+    assert O.rel_l2(y, z["y_orig_f64"]) < 1e-12
+    assert O.rel_l2(inter["P"], z["P_f64"]) < 1e-12
+    assert O.rel_l2(inter["Hol"], z["Hol_f64"]) < 1e-12
+    y32 = O.forward_general(p, x, int(z["H"]), float(z["edge_scale"]), mask, str(z["mode"]),
+                            str(z["link_mode"]), np.float32)
+    assert O.rel_l2(y32, z["y_orig_f64"]) < 1e-5
+
+
+def test_wrap_pairs_need_hol_not_its_transpose():
+    """With the wrap pairs live (no mask), transporting them by Hol^T (as the chunked
+    module's dead branch does) is far from core/attention.py: the fixtures tell the two apart."""
+    p, x, mask, z = general_case("gen_none_es15")
+    H, es = int(z["H"]), float(z["edge_scale"])
+    _, inter = O.forward_general(p, x, H, es, mask, "causal", "interaction", np.float64,
+                                 return_intermediates=True)
+    P, Hol = inter["P"], inter["Hol"]
+    q, k, v = O.project_qkv(p, x, H)
+    PT = np.swapaxes(P, -1, -2)
+    qh, kh, vh = ((PT @ t[..., None])[..., 0] for t in (q, k, v))
+    HolT = np.swapaxes(Hol, -1, -2)[:, :, None]
+    o = O.masked_attention(qh, kh, vh, 1 / np.sqrt(x.shape[-1] // H), None,
+                           (HolT @ kh[..., None])[..., 0], (HolT @ vh[..., None])[..., 0])
+    heads = (P @ o[..., None])[..., 0]
+    y_t = heads.transpose(0, 2, 1, 3).reshape(x.shape) @ p.out.T
+    assert O.rel_l2(y_t, z["y_orig_f64"]) > 0.05
