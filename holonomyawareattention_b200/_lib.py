@@ -42,6 +42,10 @@ SIGNATURES = {
                              c_int, c_int, c_int, c_void_p]),
     "hoa_attn_tc_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_int,
                                 c_int, c_int, c_int, c_int, c_void_p]),
+    "hoa_attn_general_fwd": (c_int, [c_void_p] * 7 + [c_float, c_int, c_int, c_int, c_void_p]),
+    "hoa_chain_matvec": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p]),
+    "hoa_apply_paths": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int,
+                                c_void_p]),
     "hoa_compose_paths": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p]),
     "hoa_out_transport": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_int,
                                   c_int, c_int, c_int, c_void_p]),

@@ -7,12 +7,15 @@ core/attention_fast_chunked.py:37-60, 98).  The reference's experiments pick
 the module by import path (`--attn-module`, experiments/session_cherry.py:278,
 445), so `--attn-module holonomyawareattention_b200` selects this one.
 
-Supported inputs are those of the reference's kernel drop-in
-(kernel/attention_kernel.py:193-208): mode "causal", attn_mask exactly
-tril(L), dropout inactive, CUDA input — plus return_geometry=True, which also
-returns {"C": P, "H": Hol} as core/attention_fast_chunked.py:175-177 does (P
-materialised by hoa_compose_paths).  Anything else raises
-NotImplementedError: there is no CPU or PyTorch fallback.
+The hot path is the reference kernel drop-in's case (kernel/attention_kernel.py:
+193-208): mode "causal" with attn_mask exactly tril(L).  Every other input of
+core/attention.py also runs on libhoa, through a general fp32 path: no mask or
+any (L, L) bool mask (the wrap pairs j > i transported through the closing
+edge by Hol, core/attention.py:156-165), mode "inert" (:166-169), link_mode
+"additive" (:98-101).  return_geometry=True also returns {"C": P, "H": Hol} as
+core/attention_fast_chunked.py:175-177 does.  Dropout must be inactive and the
+input on CUDA; anything else raises NotImplementedError: there is no CPU or
+PyTorch fallback.
 
 Forward only.  The projections (qkv, edge_mlp, out) run as PyTorch GEMMs;
 everything between them — link rotations, prefix composition, transport,
@@ -94,10 +97,10 @@ class PathOrderedGeometricMHA(nn.Module):
     # ------------------------------------------------------------------
     def _check_supported(self, x: torch.Tensor, attn_mask, return_geometry: bool) -> None:
         why = None
-        if self.mode != "causal":
-            why = "mode must be 'causal'"
-        elif self.link_mode != "interaction":
-            why = "link_mode must be 'interaction'"
+        if self.mode not in ("causal", "inert"):
+            why = "mode must be 'causal' or 'inert'"
+        elif self.link_mode not in ("interaction", "additive"):
+            why = "link_mode must be 'interaction' or 'additive'"
         elif not x.is_cuda:
             why = "input must be a CUDA tensor"
         elif self.training and self.dropout.p != 0.0:
@@ -106,8 +109,9 @@ class PathOrderedGeometricMHA(nn.Module):
             why = f"x must be (B, L, {self.h * self.d})"
         elif torch.is_grad_enabled() and (x.requires_grad or any(p.requires_grad for p in self.parameters())):
             why = "forward-only kernels: call under torch.no_grad() / torch.inference_mode()"
-        if why is None and not self._mask_is_tril(attn_mask, x.shape[1]):
-            why = "attn_mask must be exactly tril(L)"
+        elif attn_mask is not None and (tuple(attn_mask.shape) != (x.shape[1], x.shape[1])
+                                        or attn_mask.dtype != torch.bool):
+            why = "attn_mask must be None or an (L, L) bool tensor (True = allowed)"
         if why is not None:
             raise NotImplementedError(f"PathOrderedGeometricMHA (B200): {why}")
 
@@ -176,6 +180,10 @@ class PathOrderedGeometricMHA(nn.Module):
             partner = torch.roll(x, shifts=-1, dims=1)
         else:
             partner = torch.cat([x[:, 1:], x_next.to(x.dtype)], dim=1)
+        if self.link_mode == "additive":
+            # a_t = gq(x_t) + gk(x_{t+1}) (core/attention.py:98-101), summed in fp32
+            a = self.gqproj(x).float() + self.gkproj(partner).float()
+            return a.contiguous(), None, "packed"
         pair = torch.cat([x, partner], dim=-1)
         lin0 = self.edge_mlp[0]
         layout = self._gen_layout()
@@ -254,6 +262,10 @@ class PathOrderedGeometricMHA(nn.Module):
         self._check_supported(x, attn_mask, return_geometry)
         B, L, D = x.shape
         rows = max(1, self.PIECE_TOKENS // L)
+        # the hot path: causal mode under exactly tril(L); everything else (no mask,
+        # any other mask, the inert ablation) takes the general fp32 path
+        general = not (self.mode == "causal" and self._mask_is_tril(attn_mask, L))
+        mask = attn_mask.to(x.device) if (general and attn_mask is not None) else None
         if return_geometry:
             # {"C": P (B,H,L,d,d), "H": Hol (B,H,d,d)} in x's dtype, as
             # core/attention_fast_chunked.py:175-177 returns them
@@ -262,23 +274,32 @@ class PathOrderedGeometricMHA(nn.Module):
             Hol = torch.empty(B, self.h, self.d, self.d, dtype=x.dtype, device=x.device)
             for b0 in range(0, B, rows):
                 sl = slice(b0, min(B, b0 + rows))
-                y[sl], P[sl], Hol[sl] = self._forward_rows(x[sl], geometry=True)
+                y[sl], P[sl], Hol[sl] = self._forward_rows(x[sl], True, general, mask)
             return y, {"C": P, "H": Hol}
         if rows >= B:
-            return self._forward_rows(x), None
+            return self._forward_rows(x, False, general, mask), None
         y = torch.empty(B, L, D, dtype=x.dtype, device=x.device)
         for b0 in range(0, B, rows):
-            y[b0:b0 + rows] = self._forward_rows(x[b0:b0 + rows])
+            y[b0:b0 + rows] = self._forward_rows(x[b0:b0 + rows], False, general, mask)
         return y, None
 
-    def _forward_rows(self, x: torch.Tensor, geometry: bool = False):
+    def _forward_rows(self, x: torch.Tensor, geometry: bool = False, general: bool = False,
+                      mask: Optional[torch.Tensor] = None):
         qkv = self.qkv(x)
         if not qkv.is_contiguous():
             qkv = qkv.contiguous()
         a_all, a_bias, layout = self._edge_generators_nobias(x)
-        if geometry:
+        if geometry or general:
             B, L, _ = x.shape
             chunk = self.chunk or ops.plan_chunk(B, self.h, L, self.d, x.device)
+        if general:
+            r = ops.core_general(a_all, qkv, self.h, self.edge_scale, self.scale, x.dtype, chunk,
+                                 self.mode, mask, a_bias, layout, geometry)
+            if geometry:
+                heads, P, Hol = r
+                return self.out(heads), P, Hol
+            return self.out(r)
+        if geometry:
             heads, P, Hol = ops.core_geometry(a_all, qkv, self.h, self.edge_scale, self.scale,
                                               x.dtype, x.dtype, chunk, a_bias, layout)
             return self.out(heads), P, Hol

@@ -311,6 +311,92 @@ def core_geometry(a_all, qkv, n_heads, edge_scale, softmax_scale, out_dtype, hat
     return heads, P, total.view(B, H, d, d).to(geo_dtype)
 
 
+# ---------------------------------------------------------------------------
+# the general forms (any mask, wrap pairs, inert ablation), core/attention.py
+# ---------------------------------------------------------------------------
+def attn_general_fwd(qh: torch.Tensor, kh: torch.Tensor, vh: torch.Tensor, softmax_scale: float,
+                     kw: Optional[torch.Tensor] = None, vw: Optional[torch.Tensor] = None,
+                     mask: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Attention over all keys (fp32, (BH,T,d)): wrap pairs j > i use kw/vw when given;
+    mask (T,T) bool/uint8, True = allowed, None = all allowed."""
+    _need_cuda(qh, kh, vh, kw, vw, mask)
+    BH, T, d = qh.shape
+    for t, nm in ((qh, "qh"), (kh, "kh"), (vh, "vh"), (kw, "kw"), (vw, "vw")):
+        if t is not None and (t.dtype != torch.float32 or t.shape != (BH, T, d) or not t.is_contiguous()):
+            raise ValueError(f"{nm} must be a contiguous fp32 ({BH},{T},{d}) tensor")
+    if (kw is None) != (vw is None):
+        raise ValueError("kw and vw go together")
+    m8 = None
+    if mask is not None:
+        if tuple(mask.shape) != (T, T):
+            raise ValueError(f"mask must be ({T},{T})")
+        m8 = mask.to(device=qh.device, dtype=torch.uint8).contiguous()
+    o = torch.empty(BH, T, d, dtype=torch.float32, device=qh.device)
+    _lib.call("hoa_attn_general_fwd", _ptr(qh), _ptr(kh), _ptr(vh), _ptr(kw), _ptr(vw), _ptr(m8),
+              _ptr(o), float(softmax_scale), BH, T, d, _stream(qh.device))
+    return o
+
+
+def chain_matvec(x: torch.Tensor, M: torch.Tensor, transpose: bool = False) -> torch.Tensor:
+    """y_t = M x_t (or M^T x_t), x (BH,T,d) fp32, M (BH,d,d) fp32."""
+    _need_cuda(x, M)
+    BH, T, d = x.shape
+    _contig(x, "x"); _contig(M, "M")
+    y = torch.empty_like(x)
+    _lib.call("hoa_chain_matvec", _ptr(x), _ptr(M), _ptr(y), int(transpose), BH, T, d, _stream(x.device))
+    return y
+
+
+def apply_paths(x: torch.Tensor, R: torch.Tensor, C: torch.Tensor, chunk: int,
+                transpose: bool = False) -> torch.Tensor:
+    """y_t = P_t x_t (or P_t^T x_t) with P_t = R_t C_{t/chunk}; x (BH,T,d) fp32."""
+    _need_cuda(x, R, C)
+    BH, T, d = x.shape
+    _contig(x, "x")
+    y = torch.empty_like(x)
+    _lib.call("hoa_apply_paths", _ptr(x), _ptr(R), _ptr(C), int(chunk), _ptr(y), int(transpose),
+              BH, T, d, _stream(x.device))
+    return y
+
+
+def core_general(a_all, qkv, n_heads, edge_scale, softmax_scale, out_dtype, chunk, mode="causal",
+                 mask=None, a_bias=None, gen_layout="packed", geometry=False, geo_dtype=None):
+    """The core region for any mask and both modes of core/attention.py (fp32 throughout).
+
+    "causal": q^ = P^T q etc.; the wrap pairs j > i (live when the mask allows any)
+    see Hol k^_j and Hol v^_j (core/attention.py:156-165); out = P o.
+    "inert": q~ = P q etc., no wrap pairs, out = P^T o (:166-169).
+    Returns heads (B,T,D) in out_dtype, and with ``geometry`` also P (B,H,T,d,d) and
+    Hol (B,H,d,d) in geo_dtype (default out_dtype)."""
+    B, T, threeD = qkv.shape
+    H = n_heads
+    D = threeD // 3
+    d = D // H
+    R, U, M = link_local(a_all, qkv, H, edge_scale, chunk, a_bias, gen_layout)
+    C, total = carry_scan(M, want_total=True)
+    if mode == "causal":
+        qh, kh, vh = carry_apply(U, C, chunk, torch.float32)
+        wrap = mask is None or bool(torch.triu(mask.bool(), 1).any())
+        kw = chain_matvec(kh, total) if wrap else None
+        vw = chain_matvec(vh, total) if wrap else None
+        o = attn_general_fwd(qh, kh, vh, softmax_scale, kw, vw, mask)
+        heads = out_transport(o, R, C, chunk, B, H, out_dtype)
+    elif mode == "inert":
+        parts = qkv.view(B, T, H, 3, d).permute(3, 0, 2, 1, 4).float()        # (3,B,H,T,d)
+        qt, kt, vt = (apply_paths(parts[i].reshape(B * H, T, d).contiguous(), R, C, chunk)
+                      for i in range(3))
+        o = attn_general_fwd(qt, kt, vt, softmax_scale, None, None, mask)
+        heads = (apply_paths(o, R, C, chunk, transpose=True).view(B, H, T, d).permute(0, 2, 1, 3)
+                 .reshape(B, T, D).to(out_dtype))
+    else:
+        raise ValueError("mode must be 'causal' or 'inert'")
+    if not geometry:
+        return heads
+    geo_dtype = geo_dtype or out_dtype
+    P = compose_paths(R, C, chunk, geo_dtype).view(B, H, T, d, d)
+    return heads, P, total.view(B, H, d, d).to(geo_dtype)
+
+
 _GEMM_WS = {}
 _GEMM_WS_BYTES = 32 << 20
 

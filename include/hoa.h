@@ -179,6 +179,31 @@ int hoa_compose_paths(const float* R, const float* C, void* P, int p_dtype, int 
                       int chunk, void* stream);
 
 /*
+ * General forms of the module (core/attention.py:69-195) beside the causal
+ * tril path, all fp32, (B*H, T, d) row-major vectors:
+ *
+ * hoa_attn_general_fwd — softmax over all keys of a chain: o_i =
+ *   sum_j softmax_j(q^_i . key_ij * scale) value_ij / l.clamp_min(1e-20), with
+ *   key/value_ij = k^_j / v^_j for j <= i and, when kw/vw are given (both or
+ *   neither), kw_j / vw_j for the wrap pairs j > i (the arc transport through
+ *   the closing edge, core/attention.py:156-165: kw = Hol k^, vw = Hol v^).
+ *   mask: (T, T) bytes, nonzero = allowed, NULL = all allowed; masked scores
+ *   sit at -FLT_MAX as the reference's finfo.min (a fully masked row averages
+ *   uniformly, core/attention_fast_chunked.py:142-148).  d <= 128.
+ * hoa_chain_matvec — y_t = M x_t (transpose = 0) or M^T x_t, M (B*H, d, d).
+ * hoa_apply_paths — y_t = P_t x_t (transpose = 0) or P_t^T x_t with
+ *   P_t = R_t C_{t/chunk} (the inert ablation's transports,
+ *   core/attention.py:166-169).
+ */
+int hoa_attn_general_fwd(const float* qh, const float* kh, const float* vh, const float* kw,
+                         const float* vw, const unsigned char* mask, float* o, float softmax_scale,
+                         int BH, int T, int d, void* stream);
+int hoa_chain_matvec(const float* x, const float* M, float* y, int transpose, int BH, int T, int d,
+                     void* stream);
+int hoa_apply_paths(const float* x, const float* R, const float* C, int chunk, float* y, int transpose,
+                    int BH, int T, int d, void* stream);
+
+/*
  * Kernel (4): inverse transport out_t = R_t (C_{t/chunk} o_t), written to
  * out (B, T, H, d) in out_dtype — the input of the `out` projection.
  * Replaces core/attention_fast_chunked.py:171.

@@ -50,9 +50,15 @@ def test_unsupported_inputs_raise():
     with torch.no_grad():
         with pytest.raises(NotImplementedError, match="CUDA"):
             m(x, attn_mask=tril)
+    # the inert ablation is supported; a CPU input is still refused
     inert = PathOrderedGeometricMHA(32, n_heads=4, mode="inert").eval()
-    with torch.no_grad(), pytest.raises(NotImplementedError, match="causal"):
+    with torch.no_grad(), pytest.raises(NotImplementedError, match="CUDA"):
         inert(x, attn_mask=tril)
+    # masks must be (L, L) bool; an unknown link form is refused
+    m.link_mode = "other"
+    with torch.no_grad(), pytest.raises(NotImplementedError, match="link_mode"):
+        m(x, attn_mask=tril)
+    m.link_mode = "interaction"
     # return_geometry=True is supported, but the CPU input is still refused
     with torch.no_grad(), pytest.raises(NotImplementedError, match="CUDA"):
         m(x, attn_mask=tril, return_geometry=True)

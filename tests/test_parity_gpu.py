@@ -244,12 +244,17 @@ def test_deterministic_and_rejects():
     assert np.array_equal(run(m, x), run(m, x))
     L = x.shape[1]
     with torch.no_grad():
+        # other masks (and none) take the general path: they run and change the result
+        y_t = run(m, x)
+        other = tril(L).clone()
+        other[5, 0] = False
+        y_o, _ = m(x, attn_mask=other)
+        y_n, _ = m(x, attn_mask=None)
+        assert np.isfinite(y_o.cpu().numpy()).all() and np.isfinite(y_n.cpu().numpy()).all()
+        assert not np.array_equal(y_o.cpu().numpy(), y_t)
+        assert not np.array_equal(y_n.cpu().numpy(), y_t)
         with pytest.raises(NotImplementedError):
-            m(x, attn_mask=None)
-        bad = tril(L).clone()
-        bad[5, 0] = False
-        with pytest.raises(NotImplementedError):
-            m(x, attn_mask=bad)
+            m(x, attn_mask=tril(L).float())
 
 
 @pytest.mark.parametrize("precision,tol", [("split", 3e-5), ("bf16", 6e-3)])
