@@ -547,23 +547,44 @@ extern "C" const char* hoa_status_string(int st) {
   }
 }
 
+// Link-kernel CTAs resident per SM: the tensor-core kernel (d in {32, 48, 64,
+// 96}) is bound by its TMEM columns (5 d, rounded up to a power of two, of
+// 512), the SIMT kernel by its shared-memory footprint.
+static int link_ctas_per_sm(int d) {
+  if (d == 32 || d == 48 || d == 64 || d == 96) {
+    const int cols = 5 * d <= 128 ? 128 : (5 * d <= 256 ? 256 : 512);
+    return 512 / cols;
+  }
+  const int dp = padded_dim(d);
+  const size_t smem = (size_t)(4 * dp * dp + 4 * dp) * sizeof(float);
+  int per_sm = (int)(228 * 1024 / (smem + 1024));
+  return per_sm < 1 ? 1 : (per_sm > 8 ? 8 : per_sm);
+}
+
+// Chunk length: every (chain, chunk) unit is one CTA and all units are about
+// equally long, so the link kernel takes about ceil(units / slots) unit-times.
+// The planner picks the number of chunks per chain K that minimises
+// ceil(chains K / slots) (chunk + c0), c0 ~ 2 positions of per-CTA start-up,
+// over chunks of at least 16 positions: K chosen so that the last wave is
+// nearly full (at B16 T4096 H16 on 148 SMs, 1024 units in 7 waves rather than
+// 1216 in 8.2).
 extern "C" int hoa_plan_chunk(int B, int H, int T, int d, int num_sms) {
   if (T < 16) return T > 0 ? T : 1;
-  const int dp = padded_dim(d);
-  // resident units per SM, from the shared-memory footprint of the link kernel
-  const size_t smem = (size_t)(4 * dp * dp + 4 * dp) * sizeof(float);
-  int per_sm = smem > 0 ? (int)(228 * 1024 / (smem + 1024)) : 1;
-  per_sm = per_sm < 1 ? 1 : (per_sm > 8 ? 8 : per_sm);
   const long long chains = (long long)B * H;
-  const long long slots = (long long)(num_sms > 0 ? num_sms : 148) * per_sm;
-  // aim for ~8 waves of units, so that the partial last wave costs little
-  long long want = (8 * slots + chains - 1) / chains;
-  if (want < 1) want = 1;
-  long long chunk = (T + want - 1) / want;
-  chunk = ((chunk + 15) / 16) * 16;
-  if (chunk < 16) chunk = 16;
-  if (chunk > T) chunk = T;
-  return (int)chunk;
+  const long long slots = (long long)(num_sms > 0 ? num_sms : 148) * link_ctas_per_sm(d);
+  constexpr long long kStartup = 2;          // per-CTA start-up, in positions
+  long long best_cost = -1, best_chunk = T;
+  for (long long K = 1; K <= T / 16; ++K) {
+    const long long chunk = (T + K - 1) / K;
+    const long long units = chains * ((T + chunk - 1) / chunk);
+    const long long waves = (units + slots - 1) / slots;
+    const long long cost = waves * (chunk + kStartup);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best_chunk = chunk;
+    }
+  }
+  return (int)best_chunk;
 }
 
 namespace hoa {

@@ -64,7 +64,8 @@ const char* hoa_status_string(int status);
 
 /* Chunk length used to split each (b,h) rotation chain into independent
  * chunks (composed locally, then joined by hoa_carry_scan).  `num_sms` is the
- * device's SM count.  Returns a multiple of 16 in [16, T] (or T when T < 16). */
+ * device's SM count.  Returns a length in [16, T] (T when T < 16) chosen so
+ * that the link kernel's (chain, chunk) units fill whole waves of the GPU. */
 int hoa_plan_chunk(int B, int H, int T, int d, int num_sms);
 
 /* Floats per head of the generator row: d(d-1)/2 (banked = 0) or the banked

@@ -44,10 +44,26 @@ def test_library_facts(lib):
                                           (128, 24, 2048, 120, 148), (1, 16, 65536, 96, 148),
                                           (2, 4, 12, 8, 148), (1, 1, 1, 8, 148)])
 def test_plan_chunk(lib, B, H, T, d, sms):
+    """The chunk minimises ceil(units / slots) * (chunk + 2) over chunks of >= 16 positions
+    (units = B*H*ceil(T/chunk), slots = SMs x link CTAs per SM): the last wave stays full."""
     c = lib.hoa_plan_chunk(B, H, T, d, sms)
     assert 1 <= c <= max(T, 1)
-    if T >= 16:
-        assert c % 16 == 0 or c == T
+    if T < 16:
+        assert c == T
+        return
+    per_sm = 512 // (128 if 5 * d <= 128 else (256 if 5 * d <= 256 else 512)) \
+        if d in (32, 48, 64, 96) else None
+
+    def cost(chunk, slots):
+        units = B * H * (-(-T // chunk))
+        return -(-units // slots) * (chunk + 2)
+
+    if per_sm is not None:
+        slots = sms * per_sm
+        best = min(cost(-(-T // K), slots) for K in range(1, T // 16 + 1))
+        assert c >= 16 and cost(c, slots) == best
+        if B * H * T >= 100 * slots:          # large problems: within 5% of a perfect split
+            assert cost(c, slots) <= 1.05 * (B * H * T / slots) + 2 * -(-B * H * T // (slots * c))
 
 
 def test_workspace_bytes(lib):
