@@ -198,16 +198,11 @@ class PathOrderedGeometricMHA(nn.Module):
                                        (L if x_next is None else None))
         p2 = pair.reshape(B * L, 2 * D)
         h = torch.addmm(lin0.bias.float(), p2, lin0.weight.t(), out_dtype=torch.float32)
-        h = F.gelu(h)
-        F4 = h.shape[1]
-        # GEMM operand [h_hi | h_lo] ("bf16": h_hi) against [W2^T ; W2^T] (W2^T): W2 h_hi +
-        # W2 h_lo in fp32, the bias added in the GEMM's epilogue (hoa_edge_gemm, cuBLASLt)
-        nk = (2 if split else 1) * F4
-        lhs = torch.empty(B * L, nk, dtype=torch.bfloat16, device=x.device)
-        hi = lhs[:, :F4]
-        hi.copy_(h)
-        if split:
-            lhs[:, F4:].copy_(h.sub_(hi))
+        # GEMM operand [g_hi | g_lo] ("bf16": g_hi), g = GELU(h), in one pass (hoa_edge_gelu_split),
+        # against [W2^T ; W2^T] (W2^T): W2 g_hi + W2 g_lo in fp32, the bias added in the GEMM's
+        # epilogue (hoa_edge_gemm, cuBLASLt)
+        lhs = ops.edge_gelu_split(h, split)
+        del h
         wt, bias = self._stacked_w2t(split)
         a = ops.edge_gemm(lhs, wt, bias)
         return a.view(B, L, -1), None, layout

@@ -101,3 +101,54 @@ extern "C" int hoa_edge_gemm(const void* hidden, const void* wt, const float* bi
                      &plan.algo, workspace, plan.ws, reinterpret_cast<cudaStream_t>(stream));
   return st == CUBLAS_STATUS_SUCCESS ? HOA_OK : HOA_ERR_LAUNCH;
 }
+
+// ---------------------------------------------------------------------------
+// The edge MLP's hidden layer between its two GEMMs: g = GELU(h) (exact erf,
+// nn.GELU(), core/attention_fast_chunked.py:56-58; evaluated as
+// x * 0.5 * (1 + erf(x / sqrt 2)) in fp32, the expression PyTorch's GELU uses),
+// written as the bf16 operand of the second GEMM: [g_hi] or, split, [g_hi | g_lo]
+// with g_hi = bf16(g) and g_lo = bf16(g - g_hi).  One pass over h instead of a
+// GELU pass, a rounding copy and (split) a subtraction and a second copy.
+namespace {
+
+__global__ void edge_gelu_split_kernel(const float* __restrict__ h, __nv_bfloat16* __restrict__ out,
+                                       long long rows, int cols, int split) {
+  const int c4 = cols >> 2;
+  const long long n4 = rows * c4;
+  const float kAlpha = 0.70710678118654752440f;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / c4;
+    const int c = (int)(i % c4) * 4;
+    const float4 x = *reinterpret_cast<const float4*>(h + r * cols + c);
+    const float xv[4] = {x.x, x.y, x.z, x.w};
+    uint32_t hw[4], lw[4];                           // bf16 bit patterns
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float g = xv[k] * 0.5f * (1.0f + erff(xv[k] * kAlpha));
+      const __nv_bfloat16 hb = __float2bfloat16_rn(g);
+      hw[k] = __bfloat16_as_ushort(hb);
+      lw[k] = __bfloat16_as_ushort(__float2bfloat16_rn(g - __bfloat162float(hb)));
+    }
+    const long long ld = split ? 2LL * cols : cols;
+    __nv_bfloat16* o = out + r * ld + c;
+    *reinterpret_cast<uint2*>(o) = make_uint2(hw[0] | (hw[1] << 16), hw[2] | (hw[3] << 16));
+    if (split)
+      *reinterpret_cast<uint2*>(o + cols) = make_uint2(lw[0] | (lw[1] << 16), lw[2] | (lw[3] << 16));
+  }
+}
+
+}  // namespace
+
+extern "C" int hoa_edge_gelu_split(const float* h, void* out, long long rows, int cols, int split,
+                                   void* stream) {
+  if (!h || !out || rows < 1 || cols < 4 || (cols & 3) != 0) return HOA_ERR_INVALID_ARG;
+  if ((reinterpret_cast<uintptr_t>(h) & 15) != 0 || (reinterpret_cast<uintptr_t>(out) & 7) != 0)
+    return HOA_ERR_INVALID_ARG;
+  const long long n4 = rows * (cols >> 2);
+  long long blocks = (n4 + 255) / 256;
+  if (blocks > 148LL * 64) blocks = 148LL * 64;
+  edge_gelu_split_kernel<<<(unsigned)blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      h, static_cast<__nv_bfloat16*>(out), rows, cols, split ? 1 : 0);
+  return cudaGetLastError() == cudaSuccess ? HOA_OK : HOA_ERR_LAUNCH;
+}

@@ -397,6 +397,18 @@ def core_general(a_all, qkv, n_heads, edge_scale, softmax_scale, out_dtype, chun
     return heads, P, total.view(B, H, d, d).to(geo_dtype)
 
 
+def edge_gelu_split(h: torch.Tensor, split: bool) -> torch.Tensor:
+    """GELU(h) (exact erf) of the fp32 hidden layer as the bf16 GEMM operand:
+    (rows, cols) = bf16(g), or with ``split`` (rows, 2 cols) = [bf16(g) | bf16(g - bf16(g))]."""
+    _need_cuda(h)
+    if h.dtype != torch.float32 or h.dim() != 2 or not h.is_contiguous():
+        raise ValueError("h must be a contiguous 2-D fp32 tensor")
+    rows, cols = h.shape
+    out = torch.empty(rows, (2 if split else 1) * cols, dtype=torch.bfloat16, device=h.device)
+    _lib.call("hoa_edge_gelu_split", _ptr(h), _ptr(out), rows, cols, 1 if split else 0, _stream(h.device))
+    return out
+
+
 _GEMM_WS = {}
 _GEMM_WS_BYTES = 32 << 20
 

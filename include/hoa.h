@@ -68,6 +68,15 @@ const char* hoa_status_string(int status);
  * that the link kernel's (chain, chunk) units fill whole waves of the GPU. */
 int hoa_plan_chunk(int B, int H, int T, int d, int num_sms);
 
+/*
+ * The edge MLP's hidden layer as the bf16 operand of hoa_edge_gemm:
+ * g = GELU(h) (exact erf, nn.GELU(); core/attention_fast_chunked.py:56-58) for
+ * h (rows, cols) fp32, written as out (rows, cols) = bf16(g), or with split
+ * (rows, 2 cols) = [bf16(g) | bf16(g - bf16(g))].  cols % 4 == 0, h 16-byte
+ * aligned.  No reference counterpart beyond the GELU itself.
+ */
+int hoa_edge_gelu_split(const float* h, void* out, long long rows, int cols, int split, void* stream);
+
 /* Floats per head of the generator row: d(d-1)/2 (banked = 0) or the banked
  * layout's size (banked = 1; 0 when d % 32 != 0). */
 int hoa_gen_stride(int d, int banked);

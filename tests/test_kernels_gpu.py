@@ -206,3 +206,20 @@ def test_edge_gemm_matches_torch(M, N, K, with_bias):
     ref = h.double() @ wt.double() + (b.double() if with_bias else 0.0)
     assert out.dtype == torch.float32 and out.shape == (M, N)
     assert rel_l2(out.cpu().numpy(), ref.cpu().numpy()) < 1e-6
+
+
+@pytest.mark.parametrize("rows,cols", [(1, 4), (37, 96), (300, 6144)])
+@pytest.mark.parametrize("split", [False, True])
+def test_edge_gelu_split_matches_torch(rows, cols, split):
+    """hoa_edge_gelu_split = F.gelu (exact erf) then the bf16 split, bit for bit."""
+    torch.manual_seed(rows + cols)
+    h = 3 * torch.randn(rows, cols, device=DEV)
+    out = ops.edge_gelu_split(h, split)
+    g = torch.nn.functional.gelu(h)
+    hi = g.to(torch.bfloat16)
+    assert torch.equal(out[:, :cols], hi)
+    if split:
+        assert out.shape == (rows, 2 * cols)
+        assert torch.equal(out[:, cols:], (g - hi.float()).to(torch.bfloat16))
+    else:
+        assert out.shape == (rows, cols)
