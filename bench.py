@@ -449,7 +449,9 @@ def run_ours(args):
         "roofline": roofline, "cpu_baseline": cpu,
         "e2e": {"value": world * B * T / (e2e_ms / 1e3), "unit": "tokens/s",
                 "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes},
-        "gpu_launches": 5 * pieces * args.steps, "clocks": clk,
+        # per batch piece: link, carry scan, carry apply, attention, inverse transport, and the
+        # fused GELU of the edge MLP in bf16 (the GEMMs are cuBLAS / cuBLASLt kernels)
+        "gpu_launches": (5 + (dtype == torch.bfloat16)) * pieces * args.steps, "clocks": clk,
         "generator_precision": generator_precision_label(mod, T, dtype),
         **extra,
     }
@@ -568,7 +570,10 @@ def run_seq_sharded(args):
         "e2e": {"value": B * T / (e2e_ms / 1e3), "unit": "tokens/s",
                 "h2d_bytes_per_step": xs.numel() * xs.element_size(),
                 "d2h_bytes_per_step": xs.numel() * xs.element_size()},
-        "gpu_launches": 6 * args.steps, "clocks": clk,
+        # per step: link, two carry scans, carry apply, one attention per local segment,
+        # inverse transport, and the fused GELU of the edge MLP in bf16
+        "gpu_launches": (5 + len(seqshard.segments_of(layout, world, rank)[0])
+                         + (dtype == torch.bfloat16)) * args.steps, "clocks": clk,
         "generator_precision": generator_precision_label(mod, T, dtype),
     }
     if rank == 0:
