@@ -197,7 +197,8 @@ class PathOrderedGeometricMHA(nn.Module):
         split = self._split_generators(seq_len if seq_len is not None else
                                        (L if x_next is None else None))
         p2 = pair.reshape(B * L, 2 * D)
-        h = torch.addmm(lin0.bias.float(), p2, lin0.weight.t(), out_dtype=torch.float32)
+        w1t, b1 = self._w1t()
+        h = ops.edge_gemm(p2, w1t, b1)            # fp32 out, the bias added in the epilogue
         # GEMM operand [g_hi | g_lo] ("bf16": g_hi), g = GELU(h), in one pass (hoa_edge_gelu_split),
         # against [W2^T ; W2^T] (W2^T): W2 g_hi + W2 g_lo in fp32, the bias added in the GEMM's
         # epilogue (hoa_edge_gemm, cuBLASLt)
@@ -233,6 +234,17 @@ class PathOrderedGeometricMHA(nn.Module):
             self._b2f = br.float().contiguous()
             self._w2cat_key = key
         return self._w2cat, self._b2f
+
+    def _w1t(self):
+        """(W1^T (2D x 4D) in bf16, b1 in fp32) of the edge MLP's first layer, cached until
+        edge_mlp.0 changes."""
+        lin0 = self.edge_mlp[0]
+        w, b = lin0.weight, lin0.bias
+        key = (w.data_ptr(), w._version, b.data_ptr(), b._version, w.dtype, str(w.device))
+        if getattr(self, "_w1t_key", None) != key:
+            self._w1t_cache = (w.detach().t().to(torch.bfloat16).contiguous(), b.detach().float().contiguous())
+            self._w1t_key = key
+        return self._w1t_cache
 
     def _w2f32(self):
         """(W2, b2) in fp32 with rows in the banked layout, cached until edge_mlp.2 changes."""
