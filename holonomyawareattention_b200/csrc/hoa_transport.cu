@@ -11,7 +11,7 @@
 
 namespace hoa {
 
-constexpr int kXWarps = 8;
+constexpr int kXWarps = 16;     // 16 warps x 128 positions per CTA: measured best of 4-32 warps, 32-128 positions
 
 // y = Mat x for a compile-time d (multiple of 4): 4 rows per pass, 8 lanes per
 // row with float4 loads; the passes are unrolled in groups of 4 so that 12
@@ -96,7 +96,7 @@ HOA_DEVICE void warp_matvec(const float* __restrict__ Mat, const float* __restri
 // chunk, so that the chunk's carry C_k is read from global memory once per
 // CTA (into shared memory, rows padded to d+1 words) instead of once per
 // position; only R_t streams from HBM.
-constexpr int kXPos = 64;
+constexpr int kXPos = 128;
 
 __global__ void __launch_bounds__(kXWarps * 32)
 out_transport_kernel(const float* __restrict__ o, const float* __restrict__ R,
