@@ -393,11 +393,11 @@ def run_ours(args):
     link_flops = f_rot
     tf32_issued = n_pos * 4 * 3 * 2.0 * 128 * d * d
     # DRAM traffic per launch: dram__bytes_read.sum + dram__bytes_write.sum of one ncu capture of
-    # the link kernel on c3b1 (65,536 positions, d 96, bf16 q/k/v, banked generators): 3.739e9
+    # the link kernel on c3b1 (65,536 positions, d 96, bf16 q/k/v, banked generators): 3.707e9
     # bytes, equal to its algorithmic bytes; traffic grows in proportion to the positions, so it is scaled by them.
     traffic = args.traffic
     if traffic is None and d == 96 and dtype == torch.bfloat16:
-        traffic = 3.739e9 * n_pos / 65536
+        traffic = 3.707e9 * n_pos / 65536
     roofline = {"bound": "tensor", "kernel": "link_local (kernels 1+2)",
                 "achieved": link_flops / link_s / 1e12, "peak": bf16_burst, "unit": "TFLOP/s",
                 "frac": link_flops / link_s / 1e12 / bf16_burst, "traffic": traffic,
