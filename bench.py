@@ -11,9 +11,10 @@ rotations, edge_scale 0.05), the configuration the metric is quoted on.
 With N GPUs every rank runs its own batch (batch sharding, no data-path
 collective: weak scaling); rank 0 prints one JSON line.
 
-`--impl reference` times the reference algorithm's CPU implementation (the
-numpy restatement in oracle/, float32, all host threads) on a bounded sample
-of the same workload; under torchrun only rank 0 runs it.
+`--impl reference` times the reference forward on the host's CPU cores (its
+torch restatement in oracle/torch_ref.py, float32, all host threads; the
+reference's own Python cannot travel to the GPU box) on a bounded sample of
+the same workload; under torchrun only rank 0 runs it.
 """
 from __future__ import annotations
 
@@ -120,43 +121,49 @@ def physical_gpu_index(local_rank: int) -> str:
 
 
 # ---------------------------------------------------------------------------
-# CPU baseline: the reference algorithm's CPU implementation (numpy port)
+# CPU baseline: the reference forward restated in torch (oracle/torch_ref.py,
+# the same torch operations as core/attention_fast_chunked.py, bit-identical
+# output; the reference's own Python cannot travel to the GPU box), fp32, on all
+# host cores
 # ---------------------------------------------------------------------------
-def cpu_sample_forward(sd_np, D, H, T_sample):
-    import numpy as np
-    from oracle import holonomy_oracle as O
-    rng = np.random.default_rng(0)
-    x = O.round_bf16(rng.standard_normal((1, T_sample, D)).astype(np.float32))
-    t0 = time.perf_counter()
-    O.forward(sd_np, x, H, EDGE_SCALE, np.float32)
-    return time.perf_counter() - t0
-
-
 def cpu_threads():
-    try:
-        from threadpoolctl import threadpool_info
-        n = [i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"]
-        return max(n) if n else 1
-    except Exception:
-        return os.cpu_count() or 1
+    import torch
+    return torch.get_num_threads()
 
 
-def seeded_params_np(D, H, seed=0):
-    """Weights for the CPU sample: seeded default init, bf16-rounded (the bf16 workload's values)."""
-    import numpy as np
+def cpu_sample_setup(D, H):
+    """(weights, input) of the CPU sample: seeded default init and x ~ N(0,1), both
+    bf16-rounded (the values of the bf16 workload), as fp32 CPU tensors."""
     import torch
     from oracle.seeded import seeded_state_dict
-    from oracle.holonomy_oracle import Params
-    sd = seeded_state_dict(D, H, seed)
-    sd = {k: v.to(torch.bfloat16).float() for k, v in sd.items() if not k.startswith(("gq", "gk"))}
-    return Params.from_state_dict(sd, dtype=np.float32)
+    torch.set_num_threads(os.cpu_count() or 1)
+    sd = seeded_state_dict(D, H, 0)
+    return {k: v.to(torch.bfloat16).float() for k, v in sd.items() if not k.startswith(("gq", "gk"))}
+
+
+def cpu_sample_forward(sd, D, H, T_sample):
+    """Seconds for one reference forward of one sequence of T_sample positions."""
+    import torch
+    from oracle import torch_ref
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(1, T_sample, D, generator=g).to(torch.bfloat16).float()
+    with torch.inference_mode():
+        t0 = time.perf_counter()
+        torch_ref.module_forward(sd, x, H, EDGE_SCALE, torch.float32)
+        return time.perf_counter() - t0
 
 
 def cpu_sample_len(T):
-    """Positions of the CPU sample: one sequence of up to 1024 positions (about 10 s of
-    work on the GPU host's cores at the c3 width, the cost growing with T like the
-    full workload's)."""
+    """Positions of the CPU sample: one sequence of up to 1024 positions (a few seconds on
+    the GPU host's cores at the c3 width; the cost grows with T like the full workload's)."""
     return min(T, 1024)
+
+
+def cpu_sample_desc(D, H, Ts):
+    return (f"1 sequence of T={Ts} at d_model={D}, H={H} per step: the reference forward "
+            "(core/attention_fast_chunked.py) restated in torch (oracle/torch_ref.py, output "
+            "bit-identical to the reference's on the same CPU), fp32, bf16-valued inputs and "
+            "weights")
 
 
 def run_reference_arm(args):
@@ -165,7 +172,7 @@ def run_reference_arm(args):
         return 0
     B, T, D, H, dt = CONFIGS[args.config]
     Ts = cpu_sample_len(T)
-    p = seeded_params_np(D, H)
+    p = cpu_sample_setup(D, H)
     times = []
     for i in range(args.warmup + args.steps):
         s = cpu_sample_forward(p, D, H, Ts)
@@ -180,9 +187,7 @@ def run_reference_arm(args):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic", "config": config_obj(args.config, args.gpus),
         "cpu_baseline": {"value": val, "unit": "tokens/s", "cores": cores, "kind": "port",
-                         "sample": f"1 sequence of T={Ts} at d_model={D}, H={H} per step "
-                                   "(numpy float32 restatement of the reference forward, "
-                                   "bf16-valued inputs/weights)"},
+                         "sample": cpu_sample_desc(D, H, Ts), "sample_tokens_per_step": Ts},
         "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -207,9 +212,64 @@ def config_obj(name, n, layout="zigzag"):
             "l2": "inputs and workspace (tens of GB) far exceed the 126 MB L2"}
 
 
+def cpu_baseline_leg(D, H, T):
+    """The cpu_baseline object of our arm: one warm-up and two timed samples."""
+    p = cpu_sample_setup(D, H)
+    Ts = cpu_sample_len(T)
+    cpu_sample_forward(p, D, H, min(Ts, 64))
+    sec = min(cpu_sample_forward(p, D, H, Ts) for _ in range(2))
+    return {"value": Ts / sec, "unit": "tokens/s", "cores": cpu_threads(), "kind": "port",
+            "sample": cpu_sample_desc(D, H, Ts), "sample_tokens_per_step": Ts}
+
+
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
+def measure_tf32_peak(dev):
+    """Dense tf32 tensor throughput of this GPU, TFLOP/s: cuBLAS fp32 GEMM 8192^3 with
+    tf32 allowed, best of 10 (CUDA events)."""
+    import torch
+    n = 8192
+    a = torch.randn(n, n, device=dev)
+    b = torch.randn(n, n, device=dev)
+    prev = torch.get_float32_matmul_precision()
+    torch.set_float32_matmul_precision("high")
+    try:
+        for _ in range(3):
+            a @ b
+        best = float("inf")
+        for _ in range(10):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            a @ b
+            e1.record()
+            torch.cuda.synchronize(dev)
+            best = min(best, e0.elapsed_time(e1))
+    finally:
+        torch.set_float32_matmul_precision(prev)
+    del a, b
+    return 2.0 * n ** 3 / (best / 1e3) / 1e12
+
+
+def precision_vs_fp32(mod, x1, mask):
+    """rel-L2 of the benchmarked bf16 forward against the fp32 forward of the same weights
+    on the same (bf16-valued) input, batch row 0: what the bf16 arithmetic and the generator
+    precision cost.  The fp32 path matches the reference within 1e-5 (parity tests)."""
+    import copy
+    import torch
+    m32 = copy.deepcopy(mod).float()
+    y = mod(x1, attn_mask=mask)[0].float()
+    y32 = m32(x1.float(), attn_mask=mask)[0]
+    del m32
+    q = 3 * y.shape[1] // 4
+
+    def rel(a, b):
+        return float((a - b).norm() / b.norm())
+    return {"against": "fp32 forward of the same weights and input (batch row 0)",
+            "rel_l2": rel(y, y32), "rel_l2_last_quarter": rel(y[:, q:], y32[:, q:]),
+            "bar": 2e-2}
+
+
 def generator_precision_label(mod, T, dtype):
     """The edge-MLP precision the timed forward used ("fp32" for a float32
     module; T None: a sequence shard)."""
@@ -362,6 +422,10 @@ def run_ours(args):
         if not torch.equal(yh, y_check.cpu()):
             raise RuntimeError("end-to-end output differs from the device-resident forward")
         nbytes = x.numel() * x.element_size()
+        # every launch above finished without a device-side wait giving up
+        ops.check_status(dev)
+        precision = precision_vs_fp32(mod, x[:1], mask) if dtype == torch.bfloat16 else None
+    tf32_peak = measure_tf32_peak(dev)
 
     # our kernels per forward: link, carry scan, carry apply, attention, inverse
     # transport, once per batch piece of the module's forward
@@ -375,70 +439,69 @@ def run_ours(args):
     link_bytes = n_pos * (m_dim * 4 + 3 * d * s_x + d * d * 4 + 3 * d * 4)   # a, q,k,v in; R, U out
     core_bytes = n_pos * (m_dim * 4 + 4 * d * s_x)                 # + o
     f_attn = 4.0 * B * H * d * T * (T + 1) / 2
+    # F_rot: 3 d^3 products per position for the expm (A^2, A^4, the T8 product) and one for
+    # the composition, each fp32-accurate (2 d^3 flops)
     f_rot = n_pos * 4 * 2.0 * d ** 3
     link_s = stage["link_local"] / 1e3
+    attn_s = stage[names[3]] / 1e3
     hbm = peaks["hbm_gbs"]
-    bf16_peak = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
+    bf16_burst = peaks["bf16_tflops"]
+    bf16_peak = peaks.get("bf16_tflops_sustained", bf16_burst)
     baseline_roof_s = max(f_attn / (bf16_peak * 1e12), core_bytes / (hbm * 1e9))
     sm_mhz = clk.get("sm_mhz") or 1965.0
-    ffma_peak = 148 * 128 * 2 * sm_mhz * 1e6 / 1e12
-    # The link kernel is bound by its tensor-core work (3xTF32 products) and the
-    # shared-memory traffic feeding it, not by HBM.  Algorithmic flops: the four
-    # d x d x d products per position in fp32-accurate arithmetic.  The tf32 view
-    # counts what the tensor pipe actually executes: 3 passes, M padded to 128;
-    # tf32 runs at half the bf16 rate on tcgen05 (2048 vs 4096 FMA/clk/SM, both
-    # measured with a tcgen05.mma microbenchmark), so its peak is the measured
-    # bf16 peak / 2.
-    bf16_burst = peaks["bf16_tflops"]
-    link_flops = f_rot
-    tf32_issued = n_pos * 4 * 3 * 2.0 * 128 * d * d
+    tc_link = d in (32, 48, 64, 96)
+    if tc_link:
+        # fp32-accurate products as 3xTF32: the bound is the tf32 tensor peak / 3
+        fp32acc_peak = tf32_peak / 3
+        peak_source = (f"tf32 dense peak measured in this run ({tf32_peak:.1f} TFLOP/s: cuBLAS TF32 "
+                       "GEMM 8192^3, best of 10) / 3, the 3 tf32 passes of a 3xTF32 product")
+        kname = "link_tc_kernel (hoa_link_local: kernels 1+2, tcgen05 3xTF32)"
+    else:
+        fp32acc_peak = 148 * 128 * 2 * sm_mhz * 1e6 / 1e12
+        peak_source = (f"nominal FFMA peak at the median SM clock ({sm_mhz:.0f} MHz): "
+                       "148 SMs x 128 lanes x 2 flops")
+        kname = "link_local_kernel (hoa_link_local: kernels 1+2, FFMA)"
     # DRAM traffic per launch: dram__bytes_read.sum + dram__bytes_write.sum of one ncu capture of
     # the link kernel on c3b1 (65,536 positions, d 96, bf16 q/k/v, banked generators): 3.707e9
     # bytes, equal to its algorithmic bytes; traffic grows in proportion to the positions, so it is scaled by them.
     traffic = args.traffic
     if traffic is None and d == 96 and dtype == torch.bfloat16:
         traffic = 3.707e9 * n_pos / 65536
-    roofline = {"bound": "tensor", "kernel": "link_local (kernels 1+2)",
-                "achieved": link_flops / link_s / 1e12, "peak": bf16_burst, "unit": "TFLOP/s",
-                "frac": link_flops / link_s / 1e12 / bf16_burst, "traffic": traffic,
+    rot_tflops = f_rot / link_s / 1e12
+    roofline = {"bound": "tensor", "kernel": kname,
+                "achieved": rot_tflops, "peak": fp32acc_peak, "unit": "TFLOP/s",
+                "frac": rot_tflops / fp32acc_peak, "traffic": traffic,
                 "traffic_unit": "bytes per launch (DRAM read + write)",
-                "peak_source": f"bf16_tflops (of {peaks['source']})",
-                "algorithmic_flops_per_launch": link_flops,
-                "note": "algorithmic = 4 fp32-accurate d^3 products per position; see roofline_tf32_pipe"}
+                "peak_source": peak_source,
+                "algorithmic_flops_per_launch": f_rot,
+                "definition": "F_rot = N_pos x 4 x 2 d^3 (three expm products + the composition, "
+                              "fp32-accurate) / the kernel's CUDA-event time, against the "
+                              "fp32-accurate peak"}
     extra = {
-        "roofline_tf32_pipe": {
-            "definition": "tf32 MMA flops the link kernel issues (4 products x 3 passes x 2*128*d*d per "
-                          "position) / link_local time, vs measured bf16 peak / 2",
-            "achieved_tflops": tf32_issued / link_s / 1e12, "peak_tflops": bf16_burst / 2,
-            "frac": tf32_issued / link_s / 1e12 / (bf16_burst / 2)},
+        "tf32_tflops_measured": tf32_peak,
+        "roofline_attention": {
+            "kernel": "attn_tc_kernel (hoa_attn_tc_fwd)" if tc else "attn_kernel (hoa_attn_fwd, fp32)",
+            "definition": "F_attn = 4 B H d T(T+1)/2 (causal QK^T + PV) / the kernel's time, against "
+                          "the measured bf16 burst peak",
+            "achieved_tflops": f_attn / attn_s / 1e12, "peak_tflops": bf16_burst,
+            "frac": f_attn / attn_s / 1e12 / bf16_burst},
         "roofline_link_hbm": {
             "achieved_gbs": link_bytes / link_s / 1e9, "peak_gbs": hbm,
             "frac": link_bytes / link_s / 1e9 / hbm, "algorithmic_bytes_per_launch": link_bytes},
         "core_ms_per_step": core, "stage_ms": stage, "chunk": chunk,
         "roofline_baseline_formula": {
-            "definition": "max(F_attn / bf16 peak, (a_all fp32 + q,k,v,o) bytes / HBM BW) over the core region",
+            "definition": "max(F_attn / bf16 peak (sustained), (a_all fp32 + q,k,v,o) bytes / HBM BW) "
+                          "over the core region",
             "target_ms": baseline_roof_s * 1e3, "core_ms": core, "frac": baseline_roof_s * 1e3 / core},
         "roofline_extended": {
-            "definition": "max(that, F_rot / (tf32 peak / 3)): fp32-accurate rotations as 3xTF32, "
-                          "tf32 peak = measured bf16 peak / 2",
-            "target_ms": max(baseline_roof_s, f_rot / (bf16_burst / 2 / 3 * 1e12)) * 1e3,
+            "definition": "max(that, F_rot / fp32-accurate peak) over the core region",
+            "target_ms": max(baseline_roof_s, f_rot / (fp32acc_peak * 1e12)) * 1e3,
             "core_ms": core,
-            "frac": max(baseline_roof_s, f_rot / (bf16_burst / 2 / 3 * 1e12)) * 1e3 / core},
-        "roofline_fp32_rotations": {
-            "definition": "F_rot = N_pos * 4 * 2 d^3 (3 expm products + 1 composition) / link_local time, "
-                          "vs FFMA peak 148 SM x 128 lanes x 2 x median SM clock (nominal, not measured)",
-            "achieved_tflops": f_rot / link_s / 1e12, "peak_tflops": ffma_peak,
-            "frac": f_rot / link_s / 1e12 / ffma_peak},
+            "frac": max(baseline_roof_s, f_rot / (fp32acc_peak * 1e12)) * 1e3 / core},
     }
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        p = seeded_params_np(D, H)
-        Ts = cpu_sample_len(T)
-        cpu_sample_forward(p, D, H, min(Ts, 32))
-        sec = cpu_sample_forward(p, D, H, Ts)
-        cpu = {"value": Ts / sec, "unit": "tokens/s", "cores": cpu_threads(), "kind": "port",
-               "sample": f"1 sequence of T={Ts} at d_model={D}, H={H} (numpy float32 restatement "
-                         "of the reference forward, bf16-valued inputs/weights)"}
+        cpu = cpu_baseline_leg(D, H, T)
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
@@ -453,6 +516,7 @@ def run_ours(args):
         # fused GELU of the edge MLP in bf16 (the GEMMs are cuBLAS / cuBLASLt kernels)
         "gpu_launches": (5 + (dtype == torch.bfloat16)) * pieces * args.steps, "clocks": clk,
         "generator_precision": generator_precision_label(mod, T, dtype),
+        "precision_rel_l2": precision,
         **extra,
     }
     if rank == 0:
@@ -488,7 +552,7 @@ def run_seq_sharded(args):
                                 device_id=dev)
     else:
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
-    from holonomyawareattention_b200 import PathOrderedGeometricMHA, seqshard
+    from holonomyawareattention_b200 import PathOrderedGeometricMHA, ops, seqshard
 
     B, T, D, H, dtn = CONFIGS[args.config]
     dtype = torch.bfloat16 if dtn == "bf16" else torch.float32
@@ -538,6 +602,7 @@ def run_seq_sharded(args):
         t2 = torch.tensor([f0.elapsed_time(f1) / args.steps], dtype=torch.float64, device=dev)
         dist.all_reduce(t2, op=dist.ReduceOp.MAX)
         e2e_ms = float(t2.item())
+        ops.check_status(dev)
     peaks = load_peaks()
     n_pos = B * H * T
     m_dim = d * (d - 1) // 2
@@ -547,13 +612,7 @@ def run_seq_sharded(args):
     roof_s = max(f_attn / (bf16_peak * 1e12 * world), core_bytes / (peaks["hbm_gbs"] * 1e9 * world))
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        p = seeded_params_np(D, H)
-        Ts = cpu_sample_len(T)
-        cpu_sample_forward(p, D, H, min(Ts, 32))
-        sec = cpu_sample_forward(p, D, H, Ts)
-        cpu = {"value": Ts / sec, "unit": "tokens/s", "cores": cpu_threads(), "kind": "port",
-               "sample": f"1 sequence of T={Ts} at d_model={D}, H={H} (numpy float32 restatement "
-                         "of the reference forward, bf16-valued inputs/weights)"}
+        cpu = cpu_baseline_leg(D, H, T)
     line = {
         "metric": METRIC, "value": B * T / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,

@@ -32,7 +32,7 @@ SIGNATURES = {
                                  c_float, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
                                  c_void_p, c_size_t, c_void_p]),
     "hoa_link_local": (c_int, [c_void_p, c_int, c_void_p, c_float, c_void_p, c_int, c_void_p, c_void_p,
-                               c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p]),
+                               c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p]),
     "hoa_carry_scan": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
                                c_void_p]),
     "hoa_carry_apply": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,
@@ -53,6 +53,8 @@ SIGNATURES = {
     "hoa_core_forward_noalloc": (c_int, [c_void_p, c_int, c_void_p, c_float, c_void_p, c_int, c_void_p, c_int,
                                          c_int, c_float, c_void_p, c_void_p, c_int, c_int, c_int,
                                          c_int, c_int, c_void_p]),
+    "hoa_noalloc_status_word": (c_int, [ctypes.POINTER(c_void_p)]),
+    "hoa_set_wait_bound": (c_int, [ctypes.c_longlong]),
     "hoa_selftest_wait": (c_int, [c_void_p, ctypes.c_longlong, c_void_p]),
     "hoa_edge_gemm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p,
                               c_size_t, c_void_p]),

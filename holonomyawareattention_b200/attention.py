@@ -267,6 +267,9 @@ class PathOrderedGeometricMHA(nn.Module):
     def forward(self, x: torch.Tensor, attn_mask: Optional[torch.Tensor] = None,
                 return_geometry: bool = False):
         self._check_supported(x, attn_mask, return_geometry)
+        # an earlier launch on this device whose device-side wait gave up raises here
+        # (ops.check_status() waits for the launches still running and raises too)
+        ops.poll_status(x.device)
         B, L, D = x.shape
         rows = max(1, self.PIECE_TOKENS // L)
         # the hot path: causal mode under exactly tril(L); everything else (no mask,

@@ -59,6 +59,7 @@ struct AttnTcArgs {
   int* status;
   int Tq, Tk, q_offset, d;   // query rows are global positions q_offset .. q_offset + Tq - 1
   float scale_log2;
+  long long max_wait;        // bound of the abortable waits, SM cycles (wait_bound_cycles())
 };
 
 HOA_DEVICE uint32_t pack_bf16x2(float lo, float hi) {
@@ -131,7 +132,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
       int issued[2] = {0, 0};
       for (int j = 0; j < nkt; ++j) {
         const int s = j & 1;
-        if (j >= 2 && !mbar_wait_abortable(&kv_empty[s], ((j >> 1) - 1) & 1, s_abort)) { bad = true; break; }
+        if (j >= 2 && !mbar_wait_abortable(&kv_empty[s], ((j >> 1) - 1) & 1, s_abort, p.max_wait)) { bad = true; break; }
         uint8_t* st = sm + L::offStage + s * L::kStage;
         mbar_arrive_expect_tx(&kv_full[s], kq + v_bytes);
         for (int kb = 0; kb < L::NKB; ++kb) tma_load_3d(st + kb * L::kBlk, &tk, &kv_full[s], kb * 64, j * 128, chain);
@@ -154,10 +155,10 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
       const uint64_t dQ[2] = {desc_sw128(smem_u32(sm + L::offQ)), desc_sw128(smem_u32(sm + L::offQ + L::kQ))};
       const uint32_t colS[2] = {tmem + L::colS0, tmem + L::colS1};
       const uint32_t colO[2] = {tmem + L::colO0, tmem + L::colO1};
-      bool ok = mbar_wait_abortable(q_full, 0, s_abort);
+      bool ok = mbar_wait_abortable(q_full, 0, s_abort, p.max_wait);
       for (int j = 0; j < nkt && ok; ++j) {
         const int s = j & 1;
-        ok = mbar_wait_abortable(&kv_full[s], (j >> 1) & 1, s_abort);
+        ok = mbar_wait_abortable(&kv_full[s], (j >> 1) & 1, s_abort, p.max_wait);
         if (!ok) break;
         tc_fence_after();
         const uint32_t st = smem_u32(sm + L::offStage + s * L::kStage);
@@ -175,7 +176,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
 #pragma unroll
         for (int i = 0; i < 2; ++i) {
           if (j >= n_t[i] || !ok) continue;
-          ok = mbar_wait_abortable(&p_full[i], j & 1, s_abort);
+          ok = mbar_wait_abortable(&p_full[i], j & 1, s_abort, p.max_wait);
           if (!ok) break;
           tc_fence_after();
 #pragma unroll
@@ -204,7 +205,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
     const float c = p.scale_log2;
     float m_ref = -INFINITY, l_run = 0.f;
     for (int j = 0; j < ni; ++j) {
-      bad |= !mbar_wait_abortable(&s_full[i], j & 1, s_abort);
+      bad |= !mbar_wait_abortable(&s_full[i], j & 1, s_abort, p.max_wait);
       tc_fence_after();
       const int k0 = j * 128;
       const bool diag = k0 + 127 > qi || k0 + 127 >= Tk;          // some key of the tile masked
@@ -231,7 +232,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
       const float corr = move ? exp2f(m_ref - m_new) : 1.f;        // 0 on the first tile
       if (__any_sync(0xffffffffu, move) && j > 0) {
         // rescale this warp's rows of O once the previous P V has completed
-        bad |= !mbar_wait_abortable(&pv_done[i], (j - 1) & 1, s_abort);
+        bad |= !mbar_wait_abortable(&pv_done[i], (j - 1) & 1, s_abort, p.max_wait);
         tc_fence_after();
 #pragma unroll
         for (int c16 = 0; c16 < DP16 / 16; ++c16) {
@@ -270,7 +271,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
     }
     // ---- epilogue: o = O / l for the rows of this tile that exist
     if (ni > 0) {
-      bad |= !mbar_wait_abortable(&pv_done[i], (ni - 1) & 1, s_abort);
+      bad |= !mbar_wait_abortable(&pv_done[i], (ni - 1) & 1, s_abort, p.max_wait);
       tc_fence_after();
       const int lrow = (2 * pair + i) * 128 + r;     // local query row
       const float inv = 1.f / fmaxf(l_run, 1e-20f);
@@ -363,7 +364,8 @@ extern "C" int hoa_attn_tc_fwd(const void* qh, const void* kh, const void* vhT, 
       !make_map(&mk, kh, d, Tk, BH, (uint64_t)d * 2, (uint64_t)Tk * d * 2, 128) ||
       !make_map(&mv, vhT, Tk, d, BH, tp * 2, tp * d * 2, (uint32_t)d))
     return HOA_ERR_INVALID_ARG;
-  AttnTcArgs a{o, status, Tq, Tk, q_offset, d, softmax_scale * 1.4426950408889634f};
+  AttnTcArgs a{o, status, Tq, Tk, q_offset, d, softmax_scale * 1.4426950408889634f,
+               wait_bound_cycles()};
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   switch (dp16) {
     case 16: return launch_tc<16>(mq, mk, mv, a, BH, s);

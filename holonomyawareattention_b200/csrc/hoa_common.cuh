@@ -25,6 +25,11 @@ HOA_DEVICE void store_elem(void* p, long long i, int dtype, float v) {
 
 inline int ceil_div(long long a, long long b) { return (int)((a + b - 1) / b); }
 
+// Bound, in SM cycles, of the abortable device-side waits of the kernels
+// launched from now on (hoa_set_wait_bound; the library default unless a test
+// shortened it).  Defined in hoa_link.cu.
+long long wait_bound_cycles();
+
 // Record the first device-side failure so that the host can read it later.
 inline int launch_status() {
   cudaError_t e = cudaGetLastError();

@@ -12,7 +12,9 @@
 // Arithmetic is fp32 throughout (FFMA).  Each unit keeps four d x d matrices
 // in shared memory: the running local product R, the generator A (later G^T),
 // and two operand buffers.  Each thread owns a TM x TN tile of every product.
-#include "hoa_common.cuh"
+#include <atomic>
+
+#include "hoa_sm100.cuh"
 
 namespace hoa {
 
@@ -518,7 +520,19 @@ using namespace hoa;
 
 static bool valid_dtype(int t) { return t == HOA_F32 || t == HOA_BF16; }
 
-extern "C" int hoa_abi_version(void) { return 1; }
+extern "C" int hoa_abi_version(void) { return 2; }
+
+// Process-wide bound of the abortable device-side waits (hoa_set_wait_bound).
+// Read at each launch of a kernel with such waits and passed as an argument.
+static std::atomic<long long> g_wait_bound{sm100::kMaxWaitCycles};
+
+long long hoa::wait_bound_cycles() { return g_wait_bound.load(std::memory_order_relaxed); }
+
+extern "C" int hoa_set_wait_bound(long long max_cycles) {
+  if (max_cycles < 0 || max_cycles > sm100::kMaxWaitCycles) return HOA_ERR_INVALID_ARG;
+  g_wait_bound.store(max_cycles == 0 ? sm100::kMaxWaitCycles : max_cycles, std::memory_order_relaxed);
+  return HOA_OK;
+}
 
 extern "C" int hoa_gen_stride(int d, int banked) {
   if (d < 2) return 0;
@@ -623,8 +637,9 @@ static int link_local_dispatch(const void* a_all, int a_dtype, const float* a_bi
 
 extern "C" int hoa_link_local(const void* a_all, int a_dtype, const float* a_bias,
                               float edge_scale, const void* qkv, int qkv_dtype, float* R, float* U,
-                              float* M, int B, int H, int T, int d, int chunk, void* stream) {
-  return link_local_dispatch(a_all, a_dtype, a_bias, edge_scale, qkv, qkv_dtype, R, U, M, nullptr,
+                              float* M, int* status, int B, int H, int T, int d, int chunk,
+                              void* stream) {
+  return link_local_dispatch(a_all, a_dtype, a_bias, edge_scale, qkv, qkv_dtype, R, U, M, status,
                              B, H, T, d, chunk, stream);
 }
 

@@ -102,6 +102,7 @@ struct LinkTcArgs {
   float* R; float* U; float* M;
   int* status;
   int B, H, T, chunk, K;
+  long long max_wait;   // bound of the abortable waits, SM cycles (wait_bound_cycles())
 };
 
 // Write 8 values of row `row`, columns [c0, c0+8), as tf32 hi (rounded) and
@@ -325,7 +326,7 @@ __global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, 1) link_tc_kernel(Link
                      dYlo = desc_sw128(sYlo);
       // waits for chunk j of the set, then issues that chunk of the product
       auto wait_chunk = [&](uint64_t* set, uint32_t& ph, int j) {
-        const bool ok = mbar_wait_abortable(&set[j], (ph >> j) & 1u, s_abort);
+        const bool ok = mbar_wait_abortable(&set[j], (ph >> j) & 1u, s_abort, p.max_wait);
         ph ^= 1u << j;
         if (ok) tc_fence_after();
         return ok;
@@ -397,10 +398,15 @@ __global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, 1) link_tc_kernel(Link
     };
     uint32_t ph_a[2] = {0, 0};
     uint32_t pend = 0;                      // thread 0: stages with a copy in flight
+    // A stage stays marked in flight until its wait has seen the copy land: after
+    // an abort the drain below waits for it with the full bound.
     auto wait_stage = [&](int s) {
-      bad |= !mbar_wait_abortable(&bar_a[s], ph_a[s], s_abort);
-      ph_a[s] ^= 1;
-      pend &= ~(1u << s);
+      const bool ok = mbar_wait_abortable(&bar_a[s], ph_a[s], s_abort, p.max_wait);
+      bad |= !ok;
+      if (ok) {
+        ph_a[s] ^= 1;
+        pend &= ~(1u << s);
+      }
     };
     // the generator bias of this chain's head (read through the cache: every
     // CTA of the head reads the same m floats)
@@ -549,7 +555,7 @@ __global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, 1) link_tc_kernel(Link
     };
     uint32_t ph_p1 = 0, ph_mma = 0, ph_p4 = 0;
     auto wait_done = [&](uint64_t* bar, uint32_t& ph) {
-      bad |= !mbar_wait_abortable(bar, ph, s_abort);
+      bad |= !mbar_wait_abortable(bar, ph, s_abort, p.max_wait);
       ph ^= 1;
       tc_fence_after();
     };
@@ -701,7 +707,9 @@ __global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, 1) link_tc_kernel(Link
         Ug[DP + r] = s1;
         Ug[2 * DP + r] = s2;
       }
-      if (tid == 0 && t + 2 < t1) {                       // stage sidx is free: position t + 2
+      // stage sidx is free: position t + 2 (no new copy once a wait has given up:
+      // the stage may still hold a copy in flight, which the drain waits for)
+      if (tid == 0 && t + 2 < t1 && !bad && *s_abort == 0) {
         fence_proxy_async_smem();
         fetch(sidx, t + 2);
         pend |= 1u << sidx;
@@ -886,7 +894,7 @@ int link_local_tc(const void* a_all, int a_dtype, const float* a_bias, float edg
     return HOA_ERR_UNSUPPORTED;
   const bool banked = gen_is_banked(a_dtype);
   LinkTcArgs a{static_cast<const float*>(a_all), a_bias, edge_scale, qkv, R, U, M, status,
-               B, H, T, chunk, ceil_div(T, chunk)};
+               B, H, T, chunk, ceil_div(T, chunk), wait_bound_cycles()};
   switch (d) {
     case 32: return launch_link_tc_layout<32>(a, qkv_dtype, banked, s);
     case 48: return launch_link_tc_layout<48>(a, qkv_dtype, banked, s);

@@ -7,7 +7,9 @@ tensor or an unsupported shape raises.
 """
 from __future__ import annotations
 
+import collections
 import math
+import threading
 from typing import Optional, Tuple
 
 import torch
@@ -42,6 +44,97 @@ def _contig(t: torch.Tensor, name: str) -> torch.Tensor:
     if not t.is_contiguous():
         raise ValueError(f"{name} must be contiguous")
     return t
+
+
+# ---------------------------------------------------------------------------
+# device status words.  The tensor-core kernels bound every wait on the GPU; a
+# wait that gives up makes its kernel leave early and set HOA_ERR_TIMEOUT in a
+# status word, and the output of that launch is not valid.  The word is known
+# only once the stream has run, so every op here queues a 4-byte copy of it to
+# pinned host memory behind its kernels: poll_status() raises for the copies
+# that have landed (the module calls it at every forward), check_status() waits
+# for all of them first (call it after synchronising, e.g. at the end of a run).
+# ---------------------------------------------------------------------------
+class _StatusWatch:
+    RING = 256
+
+    def __init__(self, dev: torch.device):
+        self.dev = dev
+        # the word the stage entry points share: set by a kernel, cleared here
+        self.sticky = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.host = torch.zeros(self.RING, dtype=torch.int32).pin_memory()
+        self.pending = collections.deque()        # (slot, event, what)
+        self.next = 0
+        self.lock = threading.Lock()
+
+    def watch(self, word: torch.Tensor, what: str) -> None:
+        """Queue a copy of the device int32 ``word`` behind the current stream's work."""
+        if torch.cuda.is_current_stream_capturing():
+            return
+        with self.lock:
+            if len(self.pending) == self.RING:
+                self.pending[0][1].synchronize()
+                self._poll_locked()
+            slot = self.next
+            self.next = (self.next + 1) % self.RING
+            self.host[slot:slot + 1].copy_(word.view(torch.int32)[:1], non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(torch.cuda.current_stream(self.dev))
+            self.pending.append((slot, ev, what))
+
+    def _poll_locked(self) -> None:
+        while self.pending and self.pending[0][1].query():
+            slot, _, what = self.pending.popleft()
+            st = int(self.host[slot])
+            if st != 0:
+                # report once: forget the other copies in flight and clear the shared word
+                for _, ev, _ in self.pending:
+                    ev.synchronize()
+                self.pending.clear()
+                self.sticky.zero_()
+                _lib.check(what, st)
+
+    def poll(self) -> None:
+        with self.lock:
+            self._poll_locked()
+
+    def check(self) -> None:
+        with self.lock:
+            for _, ev, _ in self.pending:
+                ev.synchronize()
+            self._poll_locked()
+
+
+_WATCH = {}
+
+
+def _watch(dev: torch.device) -> _StatusWatch:
+    dev = torch.device(dev)
+    if dev.index is None:
+        dev = torch.device("cuda", torch.cuda.current_device())
+    w = _WATCH.get(dev)
+    if w is None:
+        w = _WATCH[dev] = _StatusWatch(dev)
+    return w
+
+
+def poll_status(device=None) -> None:
+    """Raise HoaError for any finished launch on ``device`` whose device-side wait
+    gave up (HOA_ERR_TIMEOUT).  Does not wait for launches still running."""
+    _watch(device if device is not None else "cuda").poll()
+
+
+def check_status(device=None) -> None:
+    """Wait for every launch queued so far on ``device`` and raise HoaError if any
+    of them reported HOA_ERR_TIMEOUT."""
+    _watch(device if device is not None else "cuda").check()
+
+
+def set_wait_bound(max_cycles: int) -> None:
+    """Bound (SM cycles) of the device-side waits of the kernels launched from now
+    on, process-wide; 0 restores the default.  A diagnostic: a short bound makes
+    real kernels give up and report HOA_ERR_TIMEOUT (hoa_set_wait_bound)."""
+    _lib.call("hoa_set_wait_bound", int(max_cycles))
 
 
 def plan_chunk(B: int, H: int, T: int, d: int, device=None) -> int:
@@ -159,6 +252,8 @@ def core_forward(a_all: torch.Tensor, qkv: torch.Tensor, n_heads: int, edge_scal
               _ptr(qkv), _dtype_code(qkv.dtype), _ptr(out), _dtype_code(out_dtype), hat_code,
               float(softmax_scale), _ptr(carry_in), _ptr(total_out), B, H, T, d, int(chunk),
               _ptr(ws), ws_bytes, _stream(qkv.device))
+    # the status word is the workspace's first 4 bytes (hoa_core_workspace_bytes)
+    _watch(qkv.device).watch(ws[:4], "hoa_core_forward")
     return out
 
 
@@ -190,9 +285,11 @@ def link_local(a_all: torch.Tensor, qkv: torch.Tensor, n_heads: int, edge_scale:
     R = torch.empty(B * H, T, d, d, dtype=torch.float32, device=dev)
     U = torch.empty(B * H, T, 3, d, dtype=torch.float32, device=dev)
     M = torch.empty(B * H, K, d, d, dtype=torch.float32, device=dev)
+    w = _watch(dev)
     _lib.call("hoa_link_local", _ptr(a_all), a_code, _ptr(a_bias), float(edge_scale), _ptr(qkv),
-              _dtype_code(qkv.dtype), _ptr(R), _ptr(U), _ptr(M), B, H, T, d, int(chunk),
-              _stream(dev))
+              _dtype_code(qkv.dtype), _ptr(R), _ptr(U), _ptr(M), _ptr(w.sticky), B, H, T, d,
+              int(chunk), _stream(dev))
+    w.watch(w.sticky, "hoa_link_local")
     return R, U, M
 
 
@@ -257,8 +354,12 @@ def attn_tc_fwd(qh: torch.Tensor, kh: torch.Tensor, vhT: torch.Tensor, softmax_s
     if vhT.shape != (BH, d, vt_stride(Tk)):
         raise ValueError(f"v^T must be (BH, d, vt_stride(Tk)) = ({BH}, {d}, {vt_stride(Tk)})")
     o = torch.empty(BH, Tq, d, dtype=torch.float32, device=qh.device)
-    _lib.call("hoa_attn_tc_fwd", _ptr(qh), _ptr(kh), _ptr(vhT), _ptr(o), _ptr(status),
+    w = _watch(qh.device) if status is None else None
+    _lib.call("hoa_attn_tc_fwd", _ptr(qh), _ptr(kh), _ptr(vhT), _ptr(o),
+              _ptr(status) if w is None else _ptr(w.sticky),
               float(softmax_scale), BH, Tq, Tk, int(q_offset), d, _stream(qh.device))
+    if w is not None:
+        w.watch(w.sticky, "hoa_attn_tc_fwd")
     return o
 
 

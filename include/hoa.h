@@ -21,7 +21,20 @@
  * enqueued on the caller's stream (`stream` is a cudaStream_t, NULL = legacy
  * default stream).  Scratch comes from the caller through `workspace`
  * (hoa_core_workspace_bytes).  Every entry point returns a hoa_status.
- * Entry points are thread-compatible: they keep no mutable global state.
+ *
+ * Process-wide state (everything else keeps none, and may be called from
+ * several host threads on different data):
+ *   - hoa_edge_gemm keeps one cuBLASLt handle and a plan per GEMM shape, and
+ *     serialises its calls with a lock;
+ *   - hoa_core_forward_noalloc computes in one static device array per GPU,
+ *     shared by all its calls (see there), and caches that array's address
+ *     per device;
+ *   - hoa_set_wait_bound sets the bound of the device-side waits of every
+ *     kernel launched after it (a diagnostic; the default is seconds).
+ * Kernels whose bounded waits can give up report HOA_ERR_TIMEOUT through a
+ * device status word (hoa_core_forward: the first 4 bytes of the workspace;
+ * the stage entry points: their `status` argument).  The status of a launch is
+ * known only once its stream has completed: read the word then.
  */
 #ifndef HOA_H_
 #define HOA_H_
@@ -123,12 +136,14 @@ int hoa_core_forward(const void* a_all, int a_dtype, const float* a_bias, float 
  * Writes R (B*H, T, d, d) fp32 — R_t for every position —, the locally
  * transported vectors U (B*H, T, 3, d) fp32 = R_t^T [q_t, k_t, v_t], and the
  * chunk totals M (B*H, K, d, d) = R after the chunk's last edge.
+ * `status` (nullable device int) receives HOA_ERR_TIMEOUT if a bounded
+ * device-side wait gave up (the word is only ever set, never cleared).
  * Replaces core/attention_fast_chunked.py:86-94 (with core/utils.py:4-52)
  * and the transport at :108-110, split into independent chunks.
  */
 int hoa_link_local(const void* a_all, int a_dtype, const float* a_bias, float edge_scale,
                    const void* qkv, int qkv_dtype,
-                   float* R, float* U, float* M,
+                   float* R, float* U, float* M, int* status,
                    int B, int H, int T, int d, int chunk, void* stream);
 
 /*
@@ -235,11 +250,14 @@ int hoa_out_transport(const float* o, const float* R, const float* C, int chunk,
  * nothing is allocated per call.  Problems whose hoa_core_workspace_bytes
  * exceeds that size return HOA_ERR_WORKSPACE without enqueuing work.
  * It runs on the current device, and `stream` must belong to that device.
- * The first call on each device looks up the array's device address
+ * The first call on each device (and the first after a device reset, which
+ * gives the device a new context) looks up the array's device address
  * (cudaGetSymbolAddress) and caches it, so make that first call before any
  * stream capture.  All calls share the array and it keeps the last call's
  * contents: calls that overlap on the GPU (other streams, other host
- * threads) race on it, so serialise them.
+ * threads) race on it, so serialise them.  The call's device status word
+ * (0, or HOA_ERR_TIMEOUT when a bounded device-side wait gave up) is cleared
+ * at the start of every call and lies in the array: hoa_noalloc_status_word.
  */
 int hoa_core_forward_noalloc(const void* a_all, int a_dtype, const float* a_bias,
                              float edge_scale,
@@ -247,6 +265,28 @@ int hoa_core_forward_noalloc(const void* a_all, int a_dtype, const float* a_bias
                              void* out, int out_dtype, int hat_dtype, float softmax_scale,
                              const float* carry_in, float* total_out,
                              int B, int H, int T, int d, int chunk, void* stream);
+
+/*
+ * hoa_noalloc_status_word — no counterpart in the reference.  The device
+ * address, on the current device, of the status word that the last
+ * hoa_core_forward_noalloc call on that device wrote: read it (4 bytes, e.g.
+ * with cudaMemcpy) once that call's stream has completed.  Allocates nothing;
+ * like hoa_core_forward_noalloc, its first call on a device does the address
+ * look-up, so make it before any stream capture.
+ */
+int hoa_noalloc_status_word(int** dev_status);
+
+/*
+ * hoa_set_wait_bound — no counterpart in the reference.  A diagnostic: the
+ * bound, in SM cycles, of the device-side waits (on TMA and tensor-core
+ * completion) of every kernel launched after the call, process-wide.
+ * 0 restores the default (4e9 cycles, i.e. seconds); the maximum is the
+ * default.  A short bound makes a real forward's waits give up: the kernels
+ * then leave early without faulting (each waits, with the default bound, for
+ * its copies and products in flight, frees its tensor memory and returns) and
+ * report HOA_ERR_TIMEOUT in their status word; the output is not valid.
+ */
+int hoa_set_wait_bound(long long max_cycles);
 
 /*
  * hoa_edge_gemm — the second layer of the edge MLP (core/attention_fast_chunked.py:76,

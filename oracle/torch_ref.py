@@ -9,6 +9,7 @@ fixtures by tests/test_torch_ref.py.
 from __future__ import annotations
 
 import math
+from typing import Optional
 
 import torch
 import torch.nn.functional as F
@@ -73,8 +74,15 @@ def core_forward(a_all: torch.Tensor, q: torch.Tensor, k: torch.Tensor, v: torch
 
 
 def module_forward(sd: dict, x: torch.Tensor, n_heads: int, edge_scale: float,
-                   dtype=torch.float32, batch_slice: int = 1) -> torch.Tensor:
-    """Whole reference forward (causal, tril) in ``dtype`` on x's device, batch rows in slices."""
+                   dtype=torch.float32, batch_slice: int = 1,
+                   head_group: Optional[int] = None) -> torch.Tensor:
+    """Whole reference forward (causal, tril) in ``dtype`` on x's device, batch rows in slices.
+
+    ``head_group``: run the core region (expm, prefix, transport, attention)
+    over groups of this many heads at a time.  Heads never mix between the qkv
+    split and the out projection (core/attention_fast_chunked.py:69-171 works
+    per (b, h) throughout), so the result is the same; only the memory of P
+    (B, H, L, d, d) shrinks to that of one group."""
     dev = x.device
     W = {k: v.to(device=dev, dtype=dtype) for k, v in sd.items()
          if not k.startswith(("gqproj", "gkproj"))}
@@ -92,6 +100,10 @@ def module_forward(sd: dict, x: torch.Tensor, n_heads: int, edge_scale: float,
         h = F.gelu(F.linear(pair, W["edge_mlp.0.weight"], W["edge_mlp.0.bias"]))
         a = F.linear(h, W["edge_mlp.2.weight"], W["edge_mlp.2.bias"])
         a = a.view(Bb, L, H, m).transpose(1, 2)
-        heads = core_forward(a, q, k, v, edge_scale, 1.0 / math.sqrt(d))
+        hg = head_group or H
+        heads = torch.cat([core_forward(a[:, h0:h0 + hg], q[:, h0:h0 + hg], k[:, h0:h0 + hg],
+                                        v[:, h0:h0 + hg], edge_scale, 1.0 / math.sqrt(d))
+                           for h0 in range(0, H, hg)], dim=1)
+        del a, h
         ys.append(F.linear(heads.transpose(1, 2).reshape(Bb, L, D), W["out.weight"]))
     return torch.cat(ys, 0)

@@ -34,7 +34,7 @@ def test_header_symbols_exported(lib):
 
 
 def test_library_facts(lib):
-    assert lib.hoa_abi_version() == 1
+    assert lib.hoa_abi_version() == 2
     assert lib.hoa_max_head_dim() == 120
     assert lib.hoa_status_string(0) == b"ok"
     assert b"workspace" in lib.hoa_status_string(4)
@@ -76,16 +76,16 @@ def test_workspace_bytes(lib):
 def test_invalid_arguments_rejected_without_gpu(lib):
     null = None
     # null pointers -> HOA_ERR_INVALID_ARG (1) before any CUDA call
-    assert lib.hoa_link_local(null, 0, null, 1.0, null, 0, null, null, null, 1, 1, 4, 8, 4, null) == 1
+    assert lib.hoa_link_local(null, 0, null, 1.0, null, 0, null, null, null, null, 1, 1, 4, 8, 4, null) == 1
     assert lib.hoa_attn_fwd(null, null, null, 0, null, 1.0, 1, 4, 4, 0, 8, null) == 1
     assert lib.hoa_attn_tc_fwd(null, null, null, null, null, 1.0, 1, 4, 4, 0, 8, null) == 1
     assert lib.hoa_out_transport(null, null, null, 4, null, 0, 1, 1, 4, 8, null) == 1
     assert lib.hoa_carry_scan(null, null, null, null, 1, 1, 8, null) == 1
     # unsupported head dim -> HOA_ERR_UNSUPPORTED (2)
     dummy = ctypes.c_void_p(16)
-    assert lib.hoa_link_local(dummy, 0, null, 1.0, dummy, 0, dummy, dummy, dummy, 1, 1, 4, 200, 4, null) == 2
+    assert lib.hoa_link_local(dummy, 0, null, 1.0, dummy, 0, dummy, dummy, dummy, null, 1, 1, 4, 200, 4, null) == 2
     # bad dtype code
-    assert lib.hoa_link_local(dummy, 7, null, 1.0, dummy, 0, dummy, dummy, dummy, 1, 1, 4, 8, 4, null) == 2
+    assert lib.hoa_link_local(dummy, 7, null, 1.0, dummy, 0, dummy, dummy, dummy, null, 1, 1, 4, 8, 4, null) == 2
     # tensor-core attention needs d % 8 == 0 and d <= 128
     assert lib.hoa_attn_tc_fwd(dummy, dummy, dummy, dummy, null, 1.0, 1, 4, 4, 0, 12, null) == 2
     assert lib.hoa_attn_tc_fwd(dummy, dummy, dummy, dummy, null, 1.0, 1, 4, 4, 0, 136, null) == 2
@@ -95,5 +95,10 @@ def test_invalid_arguments_rejected_without_gpu(lib):
     # workspace too small -> HOA_ERR_WORKSPACE (4)
     assert lib.hoa_core_forward(dummy, 0, null, 1.0, dummy, 0, dummy, 0, 0, 1.0, null, null,
                                 1, 1, 4, 8, 4, dummy, 16, null) == 4
+    # the wait-bound diagnostic takes 0 (default) .. 4e9 cycles
+    assert lib.hoa_set_wait_bound(-1) == 1
+    assert lib.hoa_set_wait_bound(4_000_000_001) == 1
+    assert lib.hoa_set_wait_bound(0) == 0
+    assert lib.hoa_noalloc_status_word(null) == 1
     with pytest.raises(_lib.HoaError):
         _lib.check("hoa_link_local", 2)

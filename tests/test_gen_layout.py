@@ -80,9 +80,9 @@ def test_banked_layout_needs_d_multiple_of_32(lib):
     banked_f32 = _lib.HOA_F32 | _lib.HOA_GEN_BANKED
     banked_bf16 = _lib.HOA_BF16 | _lib.HOA_GEN_BANKED
     # d = 48: no banked layout; bf16 generators: no banked layout -> HOA_ERR_UNSUPPORTED
-    assert lib.hoa_link_local(dummy, banked_f32, None, 1.0, dummy, 0, dummy, dummy, dummy,
+    assert lib.hoa_link_local(dummy, banked_f32, None, 1.0, dummy, 0, dummy, dummy, dummy, None,
                               1, 1, 4, 48, 4, None) == _lib.HOA_ERR_UNSUPPORTED
-    assert lib.hoa_link_local(dummy, banked_bf16, None, 1.0, dummy, 0, dummy, dummy, dummy,
+    assert lib.hoa_link_local(dummy, banked_bf16, None, 1.0, dummy, 0, dummy, dummy, dummy, None,
                               1, 1, 4, 96, 4, None) == _lib.HOA_ERR_UNSUPPORTED
 
 

@@ -222,6 +222,52 @@ def test_config3_slice_bf16(precision):
     assert err <= BF16_TOL
 
 
+def rel_l2_whole_and_last_quarter(y, ref):
+    """rel-L2 over the whole sequence and over its last quarter, where the drift of the
+    long rotation products would show first."""
+    T = y.shape[1]
+    return O.rel_l2(y, ref), O.rel_l2(y[:, 3 * T // 4:], ref[:, 3 * T // 4:])
+
+
+def test_config3_full_batch_bf16():
+    """configs[2] at full size: all 16 batch rows (the module's forward runs them in 4 batch
+    pieces of 16K tokens) against the fp32 torch restatement on bf16-rounded inputs and weights."""
+    B, T, D, H, es = 16, 4096, 1536, 16, 0.05
+    sd, x = seeded_case(D, H, seed=0, B=B, L=T, bf16_round=True)
+    m = PathOrderedGeometricMHA(D, n_heads=H, edge_scale=es)
+    m.load_state_dict(sd)
+    m = m.to(DEV, torch.bfloat16).eval()
+    assert B * T > m.PIECE_TOKENS                      # the batch-piece loop is exercised
+    y = run(m, x.to(DEV, torch.bfloat16))
+    del m
+    torch.cuda.empty_cache()
+    ref = torch_ref.module_forward(sd, x.to(DEV), H, es, torch.float32, batch_slice=1).cpu().numpy()
+    err, err_q = rel_l2_whole_and_last_quarter(y, ref)
+    print(f"configs[2] full batch bf16: rel-L2 {err:.3e}, last quarter {err_q:.3e}")
+    assert err <= BF16_TOL and err_q <= BF16_TOL
+
+
+def test_config5_long_sequence_bf16():
+    """one sequence of T = 65536 (d_model 1536, H 16, head_dim 96, bf16) on one GPU
+    against the fp32 torch restatement (core/attention_fast_chunked.py:89-94: the sequential
+    product over 65535 edges, the drift stress of this config), run two heads at a time to
+    bound its memory.  "auto" selects the split generators at this length."""
+    B, T, D, H, es = 1, 65536, 1536, 16, 0.05
+    sd, x = seeded_case(D, H, seed=0, B=B, L=T, bf16_round=True)
+    m = PathOrderedGeometricMHA(D, n_heads=H, edge_scale=es)
+    m.load_state_dict(sd)
+    m = m.to(DEV, torch.bfloat16).eval()
+    assert m._split_generators(T)
+    y = run(m, x.to(DEV, torch.bfloat16))
+    del m
+    torch.cuda.empty_cache()
+    ref = torch_ref.module_forward(sd, x.to(DEV), H, es, torch.float32, batch_slice=1,
+                                   head_group=2).cpu().numpy()
+    err, err_q = rel_l2_whole_and_last_quarter(y, ref)
+    print(f"configs[4] T=65536 bf16: rel-L2 {err:.3e}, last quarter {err_q:.3e}")
+    assert err <= BF16_TOL and err_q <= BF16_TOL
+
+
 def test_config4_slice_bf16():
     """configs[3] shape (T=2048, d_model=2880, H=24, head_dim 120, bf16) on one batch row vs the
     fp32 torch restatement (head_dim 120 runs the FFMA link kernel)."""

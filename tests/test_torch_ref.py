@@ -19,3 +19,16 @@ def test_torch_ref_vs_golden(name):
     assert O.rel_l2(y64, z["y_chunked_f64"]) < 1e-11
     y32 = torch_ref.module_forward(sd, x, H, es, dtype=torch.float32, batch_slice=2).numpy()
     assert O.rel_l2(y32, z["y_chunked_f64"]) < 1e-5
+
+
+def test_torch_ref_head_groups_equal_all_heads():
+    """The head-group option (used to bound memory at configs[4]) gives the all-heads result:
+    heads are independent between the qkv split and the out projection."""
+    z = load("d48_L40")
+    sd, x, H, es = case_inputs(z)
+    x = torch.from_numpy(x)
+    y_all = torch_ref.module_forward(sd, x, H, es, dtype=torch.float64, batch_slice=1).numpy()
+    for hg in (1, 3):
+        y = torch_ref.module_forward(sd, x, H, es, dtype=torch.float64, batch_slice=1,
+                                     head_group=hg).numpy()
+        assert O.rel_l2(y, y_all) < 1e-14

@@ -11,6 +11,7 @@ call's contents, which must not leak into the next result), and checks that a
 problem too large for the array is refused.  The file is named so that pytest
 collects it last.
 """
+import ctypes
 import math
 
 import numpy as np
@@ -33,6 +34,19 @@ def _inputs(seed, B, T, H, d, dtype):
     return a, qkv
 
 
+def _noalloc_status(lib):
+    """The device status word of the last hoa_core_forward_noalloc call on this device
+    (hoa_noalloc_status_word), read after the stream has completed."""
+    ptr = ctypes.c_void_p()
+    assert lib.hoa_noalloc_status_word(ctypes.byref(ptr)) == 0 and ptr.value
+    torch.cuda.synchronize()
+
+    class _Word:
+        __cuda_array_interface__ = {"shape": (1,), "typestr": "<i4", "data": (ptr.value, True),
+                                    "version": 3}
+    return int(torch.as_tensor(_Word(), device=DEV).cpu()[0])
+
+
 def _noalloc(lib, a, qkv, H, d, es, chunk, dtype, out):
     B, T, _ = qkv.shape
     code = 0 if dtype == torch.float32 else 1
@@ -53,6 +67,7 @@ def test_noalloc_matches_core_forward(dtype):
         out = torch.full((B, T, H * d), float("nan"), dtype=dtype, device=DEV)
         assert _noalloc(lib, a, qkv, H, d, es, chunk, dtype, out) == 0
         torch.cuda.synchronize()
+        assert _noalloc_status(lib) == 0           # no device-side wait gave up
         assert torch.isfinite(out).all()
         assert rel_l2(out.float().cpu().numpy(), ref.float().cpu().numpy()) <= TOL[dtype]
 
