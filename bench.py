@@ -257,10 +257,12 @@ def precision_vs_fp32(mod, x1, mask):
     precision cost.  The fp32 path matches the reference within 1e-5 (parity tests)."""
     import copy
     import torch
-    m32 = copy.deepcopy(mod).float()
-    y = mod(x1, attn_mask=mask)[0].float()
-    y32 = m32(x1.float(), attn_mask=mask)[0]
-    del m32
+    # outside inference mode: the copy's weight caches track tensor versions
+    with torch.inference_mode(False), torch.no_grad():
+        m32 = copy.deepcopy(mod).float()
+        y = mod(x1, attn_mask=mask)[0].float()
+        y32 = m32(x1.float(), attn_mask=mask)[0]
+        del m32
     q = 3 * y.shape[1] // 4
 
     def rel(a, b):

@@ -60,9 +60,12 @@ class _StatusWatch:
 
     def __init__(self, dev: torch.device):
         self.dev = dev
-        # the word the stage entry points share: set by a kernel, cleared here
-        self.sticky = torch.zeros(1, dtype=torch.int32, device=dev)
-        self.host = torch.zeros(self.RING, dtype=torch.int32).pin_memory()
+        # normal tensors even when the first call comes under inference mode, so that
+        # later calls outside it may update them
+        with torch.inference_mode(False):
+            # the word the stage entry points share: set by a kernel, cleared here
+            self.sticky = torch.zeros(1, dtype=torch.int32, device=dev)
+            self.host = torch.zeros(self.RING, dtype=torch.int32).pin_memory()
         self.pending = collections.deque()        # (slot, event, what)
         self.next = 0
         self.lock = threading.Lock()

@@ -83,3 +83,18 @@ def test_stage_calls_surface_a_timed_out_wait():
         ops.set_wait_bound(0)
     ops.core_stages(a, qkv, H, 0.5, d ** -0.5, torch.bfloat16, torch.bfloat16, 64)
     ops.check_status()
+
+
+def test_status_watch_across_inference_mode():
+    """The status words of a device are first watched under inference mode, then outside it
+    (a module used for serving and for evaluation in one process)."""
+    ops._WATCH.clear()
+    B, T, H, d = 1, 64, 2, 32
+    a = (0.02 * torch.randn(B, T, H * d * (d - 1) // 2, device="cuda")).contiguous()
+    qkv = torch.randn(B, T, 3 * H * d, device="cuda").to(torch.bfloat16)
+    with torch.inference_mode():
+        ops.core_forward(a, qkv, H, 0.5)
+    with torch.no_grad():
+        ops.core_forward(a, qkv, H, 0.5)
+        ops.core_stages(a, qkv, H, 0.5, d ** -0.5, torch.bfloat16, torch.bfloat16, 16)
+    ops.check_status()

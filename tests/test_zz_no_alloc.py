@@ -42,7 +42,7 @@ def _noalloc_status(lib):
     torch.cuda.synchronize()
 
     class _Word:
-        __cuda_array_interface__ = {"shape": (1,), "typestr": "<i4", "data": (ptr.value, True),
+        __cuda_array_interface__ = {"shape": (1,), "typestr": "<i4", "data": (ptr.value, False),
                                     "version": 3}
     return int(torch.as_tensor(_Word(), device=DEV).cpu()[0])
 
