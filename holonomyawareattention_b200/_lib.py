@@ -15,7 +15,8 @@ LIB_PATH = os.path.join(_PKG, "libhoa.so")
 HOA_F32, HOA_BF16 = 0, 1
 HOA_GEN_BANKED = 0x100        # generator layout flag OR'ed into a_dtype
 # status codes (include/hoa.h)
-HOA_OK, HOA_ERR_INVALID_ARG, HOA_ERR_UNSUPPORTED, HOA_ERR_LAUNCH, HOA_ERR_WORKSPACE, HOA_ERR_TIMEOUT = range(6)
+(HOA_OK, HOA_ERR_INVALID_ARG, HOA_ERR_UNSUPPORTED, HOA_ERR_LAUNCH, HOA_ERR_WORKSPACE, HOA_ERR_TIMEOUT,
+ HOA_ERR_BOUNDS) = range(7)
 
 c_int, c_float, c_size_t, c_void_p = ctypes.c_int, ctypes.c_float, ctypes.c_size_t, ctypes.c_void_p
 
@@ -55,6 +56,7 @@ SIGNATURES = {
                                          c_int, c_int, c_void_p]),
     "hoa_noalloc_status_word": (c_int, [ctypes.POINTER(c_void_p)]),
     "hoa_set_wait_bound": (c_int, [ctypes.c_longlong]),
+    "hoa_debug_bounds": (c_int, [c_int, ctypes.POINTER(c_int)]),
     "hoa_selftest_wait": (c_int, [c_void_p, ctypes.c_longlong, c_void_p]),
     "hoa_edge_gemm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p,
                               c_size_t, c_void_p]),
@@ -72,6 +74,17 @@ class HoaError(RuntimeError):
         self.status = status
 
 
+DEBUG_LIB_PATH = os.path.join(_PKG, "libhoa_debug.so")
+
+
+def _declare(lib):
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
 def load(path: str = LIB_PATH):
     """Load libhoa.so (once) and declare every entry point's signature."""
     global _lib
@@ -82,13 +95,17 @@ def load(path: str = LIB_PATH):
             raise RuntimeError(
                 f"{path} is missing: build it with `python -m holonomyawareattention_b200._build` "
                 "(the CUDA library is the only implementation; there is no fallback)")
-        lib = ctypes.CDLL(path)
-        for name, (res, args) in SIGNATURES.items():
-            fn = getattr(lib, name)
-            fn.restype = res
-            fn.argtypes = args
-        _lib = lib
-        return lib
+        _lib = _declare(ctypes.CDLL(path))
+        return _lib
+
+
+def load_debug():
+    """A handle on libhoa_debug.so (the same C ABI, with the device-side index checks
+    of hoa_debug_bounds compiled in); separate from the product library."""
+    if not os.path.exists(DEBUG_LIB_PATH):
+        raise RuntimeError(f"{DEBUG_LIB_PATH} is missing: build it with "
+                           "`python -m holonomyawareattention_b200._build --debug-bounds`")
+    return _declare(ctypes.CDLL(DEBUG_LIB_PATH))
 
 
 def check(fn: str, status: int) -> None:

@@ -69,12 +69,15 @@ __global__ void __launch_bounds__(kAttnThreads) attn_fwd_simt_kernel(AttnArgs p)
   const int nkt = min((gq0 + kBQ - 1) / kBK, (Tk - 1) / kBK) + 1;
   const long long qbase = (long long)chain * Tq * d;
   const long long kbase = (long long)chain * Tk * d;
+  const long long BH = gridDim.y;
+  // (debug build) the query tile inside q^; a tile outside is read as zeros
+  const bool q_ok = HOA_IN(qbase + (long long)q0 * d, (long long)min(kBQ, Tq - q0) * d, BH * Tq * d);
 
   for (int i = tid; i < kBQ * DA; i += kAttnThreads) {
     const int r = i / DA, e = i % DA;
     const int t = q0 + r;
-    Qt[e * kLDT + r] = (t < Tq && e < d) ? load_elem(p.qh, qbase + (long long)t * d + e, p.hat_dtype)
-                                         : 0.f;
+    Qt[e * kLDT + r] = (t < Tq && e < d && q_ok) ? load_elem(p.qh, qbase + (long long)t * d + e, p.hat_dtype)
+                                                 : 0.f;
   }
 
   float mrow[4], lrow[4], o[4][CPT];
@@ -89,10 +92,11 @@ __global__ void __launch_bounds__(kAttnThreads) attn_fwd_simt_kernel(AttnArgs p)
   for (int kt = 0; kt < nkt; ++kt) {
     const int k0 = kt * kBK;
     __syncthreads();
+    const bool kv_ok = HOA_IN(kbase + (long long)k0 * d, (long long)min(kBK, Tk - k0) * d, BH * Tk * d);
     for (int i = tid; i < kBK * DA; i += kAttnThreads) {
       const int r = i / DA, e = i % DA;
       const int t = k0 + r;
-      const bool ok = t < Tk && e < d;
+      const bool ok = t < Tk && e < d && kv_ok;
       const long long off = kbase + (long long)t * d + e;
       Kt[e * kLDT + r] = ok ? load_elem(p.kh, off, p.hat_dtype) : 0.f;
       Vs[r * DA + e] = ok ? load_elem(p.vh, off, p.hat_dtype) : 0.f;
@@ -162,7 +166,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_fwd_simt_kernel(AttnArgs p)
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int t = q0 + r0 + i;
-    if (t >= Tq) continue;
+    if (t >= Tq || !HOA_IN(((long long)chain * Tq + t) * d, d, BH * Tq * d)) continue;
     const float inv = 1.f / fmaxf(lrow[i], 1e-20f);
     float* orow = p.o + ((long long)chain * Tq + t) * d;
 #pragma unroll

@@ -276,13 +276,16 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
       const int lrow = (2 * pair + i) * 128 + r;     // local query row
       const float inv = 1.f / fmaxf(l_run, 1e-20f);
       float* orow = p.o + ((long long)chain * p.Tq + lrow) * p.d;
+      // (debug build) the output row inside o, else not written
+      const bool o_ok = lrow < p.Tq &&
+                        HOA_IN(((long long)chain * p.Tq + lrow) * p.d, p.d, (long long)gridDim.y * p.Tq * p.d);
 #pragma unroll
       for (int c16 = 0; c16 < DP16 / 16; ++c16) {
         float ov[16];
         tmem_ld16(cO + 16 * c16, ov);
         tmem_wait_ld();
         tmem_touch(ov);
-        if (lrow < p.Tq && !bad) {
+        if (o_ok && !bad) {
 #pragma unroll
           for (int e = 0; e < 16; ++e)
             if (16 * c16 + e < p.d) orow[16 * c16 + e] = ov[e] * inv;

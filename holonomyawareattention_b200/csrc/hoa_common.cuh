@@ -25,6 +25,45 @@ HOA_DEVICE void store_elem(void* p, long long i, int dtype, float v) {
 
 inline int ceil_div(long long a, long long b) { return (int)((a + b - 1) / b); }
 
+// ---- debug bounds checks (libhoa_debug.so, -DHOA_DEBUG_BOUNDS) ----------------
+// HOA_IN(first, count, extent): the element range [first, first + count) lies in
+// [0, extent) (extent shifted right by the test hook of hoa_debug_bounds).  In
+// the debug build a failed check records HOA_ERR_BOUNDS in this translation
+// unit's debug word and the caller skips the access; the product build compiles
+// every check to `true`.
+#ifdef HOA_DEBUG_BOUNDS
+static __device__ int g_hoa_dbg_status;
+static __device__ int g_hoa_dbg_shift;
+HOA_DEVICE bool dbg_in(long long first, long long count, long long extent) {
+  if (first >= 0 && count >= 0 && first + count <= (extent >> g_hoa_dbg_shift)) return true;
+  atomicCAS(&g_hoa_dbg_status, 0, HOA_ERR_BOUNDS);
+  return false;
+}
+#define HOA_IN(first, count, extent) \
+  ::hoa::dbg_in((long long)(first), (long long)(count), (long long)(extent))
+// Each translation unit registers a host function that reads and clears its
+// debug word and sets its extent shift (hoa_debug_bounds calls them all).
+using DbgSyncFn = int (*)(int shift, int* status);
+void dbg_register(DbgSyncFn fn);
+namespace {
+int dbg_sync_tu(int shift, int* status) {
+  int st = 0, zero = 0;
+  if (cudaMemcpyFromSymbol(&st, g_hoa_dbg_status, sizeof(int)) != cudaSuccess ||
+      cudaMemcpyToSymbol(g_hoa_dbg_status, &zero, sizeof(int)) != cudaSuccess ||
+      cudaMemcpyToSymbol(g_hoa_dbg_shift, &shift, sizeof(int)) != cudaSuccess)
+    return HOA_ERR_LAUNCH;
+  if (st != 0 && *status == 0) *status = st;
+  return HOA_OK;
+}
+struct DbgRegistration {
+  DbgRegistration() { dbg_register(dbg_sync_tu); }
+};
+DbgRegistration g_dbg_registration;
+}  // namespace
+#else
+#define HOA_IN(first, count, extent) true
+#endif
+
 // Bound, in SM cycles, of the abortable device-side waits of the kernels
 // launched from now on (hoa_set_wait_bound; the library default unless a test
 // shortened it).  Defined in hoa_link.cu.

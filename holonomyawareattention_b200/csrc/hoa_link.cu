@@ -164,23 +164,30 @@ __global__ void __launch_bounds__(LinkCfg<DP>::NT, 1) link_local_kernel(LinkArgs
 
   float acc[TM][TN];
   float E[TM][TN];
+  const long long BH = (long long)p.B * p.H;
   for (int t = t0; t < t1; ++t) {
     // ---- position t: R_t and the locally transported q, k, v -------------
     const long long pos = (long long)chain * p.T + t;
-    float* Rg = p.R + pos * d * d;
-    for (int i = tid; i < d * d; i += NT) Rg[i] = bufR[(i / d) * DP + (i % d)];
     const long long qbase = (((long long)b * p.T + t) * p.H + h) * 3LL * d;
+    const long long abase = (((long long)b * p.T + t) * p.H + h) * (long long)p.a_stride;
+    // (debug build) every buffer range of this position; a failed one is skipped
+    const bool r_ok = HOA_IN(pos * d * d, d * d, BH * p.T * d * d);
+    const bool q_ok = HOA_IN(qbase, 3 * d, BH * p.T * 3 * d);
+    const bool a_ok = HOA_IN(abase, p.a_stride, BH * p.T * p.a_stride);
+    const bool u_ok = HOA_IN(pos * 3 * d, 3 * d, BH * p.T * 3 * d);
+    float* Rg = p.R + pos * d * d;
+    if (r_ok)
+      for (int i = tid; i < d * d; i += NT) Rg[i] = bufR[(i / d) * DP + (i % d)];
     for (int i = tid; i < 3 * DP; i += NT) {
       const int v = i / DP, e = i % DP;
-      svec[i] = e < d ? load_elem(p.qkv, qbase + (long long)v * d + e, p.qkv_dtype) : 0.f;
+      svec[i] = (e < d && q_ok) ? load_elem(p.qkv, qbase + (long long)v * d + e, p.qkv_dtype) : 0.f;
     }
     // ---- edge t: A = skew(edge_scale * a_t) ------------------------------
-    const long long abase = (((long long)b * p.T + t) * p.H + h) * (long long)p.a_stride;
     for (int idx = tid; idx < m; idx += NT) {
       const int i = triu_row(idx, d);
       const int j = idx - i * (2 * d - i - 1) / 2 + i + 1;
       const int slot = p.a_banked ? gen_banked_slot(i, j, d) : idx;
-      float av = load_elem(p.a, abase + slot, p.a_dtype);
+      float av = a_ok ? load_elem(p.a, abase + slot, p.a_dtype) : 0.f;
       if (p.a_bias != nullptr) av += p.a_bias[(long long)h * p.a_stride + slot];
       const float v = __fmul_rn(av, p.edge_scale);
       bufA[i * DP + j] = v;
@@ -200,7 +207,7 @@ __global__ void __launch_bounds__(LinkCfg<DP>::NT, 1) link_local_kernel(LinkArgs
       const int v = i / d, e = i % d;
       float s = 0.f;
       for (int r = 0; r < d; ++r) s = fmaf(bufR[r * DP + e], svec[v * DP + r], s);
-      Ug[i] = s;
+      if (u_ok) Ug[i] = s;
     }
 
     // ---- A2 = A A = -(A^T A); theta^2 = ||A2||_1 -------------------------
@@ -320,7 +327,8 @@ __global__ void __launch_bounds__(LinkCfg<DP>::NT, 1) link_local_kernel(LinkArgs
   }
   // chunk total: R after the chunk's last edge
   float* Mg = p.M + ((long long)chain * p.K + kc) * d * d;
-  for (int i = tid; i < d * d; i += NT) Mg[i] = bufR[(i / d) * DP + (i % d)];
+  if (HOA_IN(((long long)chain * p.K + kc) * d * d, d * d, BH * p.K * d * d))
+    for (int i = tid; i < d * d; i += NT) Mg[i] = bufR[(i / d) * DP + (i % d)];
 }
 
 // C_0 = carry_in (or I), C_{k+1} = M_k C_k.  One CTA per chain.
@@ -337,21 +345,25 @@ carry_scan_kernel(const float* __restrict__ M, const float* __restrict__ carry_i
   const int chain = blockIdx.x;
   const bool active = tid < Cf::ACTIVE;
   const int r0 = (tid / Cf::GX) * TM, c0 = (tid % Cf::GX) * TN;
+  const long long BH = gridDim.x;
+  const bool cin_ok = HOA_IN((long long)chain * d * d, d * d, BH * d * d);
 
   for (int i = tid; i < Cf::MAT; i += NT) {
     const int r = i / DP, c = i % DP;
     float v = (r == c) ? 1.f : 0.f;
-    if (carry_in != nullptr && r < d && c < d) v = carry_in[(long long)chain * d * d + r * d + c];
+    if (carry_in != nullptr && r < d && c < d && cin_ok) v = carry_in[(long long)chain * d * d + r * d + c];
     bufC[i] = v;
     bufX[i] = (r == c) ? 1.f : 0.f;
   }
   __syncthreads();
   float acc[TM][TN];
   for (int k = 0; k < K; ++k) {
+    const bool k_ok = HOA_IN(((long long)chain * K + k) * d * d, d * d, BH * K * d * d);
     float* Cg = Cout + ((long long)chain * K + k) * d * d;
-    for (int i = tid; i < d * d; i += NT) Cg[i] = bufC[(i / d) * DP + (i % d)];
+    if (k_ok)
+      for (int i = tid; i < d * d; i += NT) Cg[i] = bufC[(i / d) * DP + (i % d)];
     const float* Mg = M + ((long long)chain * K + k) * d * d;
-    for (int i = tid; i < d * d; i += NT) bufX[(i % d) * DP + (i / d)] = Mg[i];
+    for (int i = tid; i < d * d; i += NT) bufX[(i % d) * DP + (i / d)] = k_ok ? Mg[i] : 0.f;
     __syncthreads();
     zero_acc(acc);
     if (active) mm_acc<DP, TM, TN>(bufX, bufC, r0, c0, acc);
@@ -364,7 +376,7 @@ carry_scan_kernel(const float* __restrict__ M, const float* __restrict__ carry_i
     }
     __syncthreads();
   }
-  if (total_out != nullptr) {
+  if (total_out != nullptr && HOA_IN((long long)chain * d * d, d * d, BH * d * d)) {
     float* Tg = total_out + (long long)chain * d * d;
     for (int i = tid; i < d * d; i += NT) Tg[i] = bufC[(i / d) * DP + (i % d)];
   }
@@ -407,15 +419,18 @@ carry_apply_kernel(const float* __restrict__ U, const float* __restrict__ Cin, v
   const bool active = tid < Cf::ACTIVE;
   const int rg = tid / Cf::CG, cg = tid % Cf::CG;
   const int row0 = rg * TR, col0 = cg * TN;
+  const long long BH = gridDim.x / K;
   const float* Cg = Cin + ((long long)chain * K + kc) * d * d;
+  const bool c_ok = HOA_IN(((long long)chain * K + kc) * d * d, d * d, BH * K * d * d);
   for (int i = tid; i < DP * DP; i += NT) {
     const int r = i / DP, e = i % DP;
-    Cs[i] = (r < d && e < d) ? Cg[r * d + e] : 0.f;
+    Cs[i] = (r < d && e < d && c_ok) ? Cg[r * d + e] : 0.f;
   }
   // the U tile of the next step is loaded into registers while this one is computed
   float pre[Cf::kLoadPer];
   auto load_tile = [&](int tb) {
-    const int np = min(kApplyPos, t1 - tb);
+    const int np = HOA_IN(((long long)chain * T + tb) * 3 * d, (long long)min(kApplyPos, t1 - tb) * 3 * d,
+                          BH * T * 3 * d) ? min(kApplyPos, t1 - tb) : 0;   // (debug build) 0: skipped
     const float* Ug = U + ((long long)chain * T + tb) * 3 * d;
 #pragma unroll
     for (int k = 0; k < Cf::kLoadPer; ++k) {
@@ -426,7 +441,11 @@ carry_apply_kernel(const float* __restrict__ U, const float* __restrict__ Cin, v
   };
   if (t0 < t1) load_tile(t0);
   for (int tb = t0; tb < t1; tb += kApplyPos) {
-    const int np = min(kApplyPos, t1 - tb);
+    // (debug build) the hats of this tile inside their buffers, else the tile is not written
+    const int np = (HOA_IN(((long long)chain * T + tb) * d, (long long)min(kApplyPos, t1 - tb) * d, BH * T * d) &&
+                    (vt_stride == 0 || HOA_IN((long long)chain * d * vt_stride, (long long)d * vt_stride,
+                                              BH * d * vt_stride)))
+                       ? min(kApplyPos, t1 - tb) : 0;
     __syncthreads();
 #pragma unroll
     for (int k = 0; k < Cf::kLoadPer; ++k) {
@@ -528,6 +547,33 @@ static std::atomic<long long> g_wait_bound{sm100::kMaxWaitCycles};
 
 long long hoa::wait_bound_cycles() { return g_wait_bound.load(std::memory_order_relaxed); }
 
+#ifdef HOA_DEBUG_BOUNDS
+namespace {
+constexpr int kMaxDbgUnits = 32;
+hoa::DbgSyncFn g_dbg_fns[kMaxDbgUnits];
+int g_dbg_count = 0;                 // zero-initialised before any registration runs
+}  // namespace
+void hoa::dbg_register(DbgSyncFn fn) {
+  if (g_dbg_count < kMaxDbgUnits) g_dbg_fns[g_dbg_count++] = fn;
+}
+extern "C" int hoa_debug_bounds(int extent_shift, int* status) {
+  if (status == nullptr || extent_shift < 0 || extent_shift > 30) return HOA_ERR_INVALID_ARG;
+  *status = 0;
+  if (cudaDeviceSynchronize() != cudaSuccess) return HOA_ERR_LAUNCH;
+  for (int i = 0; i < g_dbg_count; ++i) {
+    const int st = g_dbg_fns[i](extent_shift, status);
+    if (st != HOA_OK) return st;
+  }
+  return HOA_OK;
+}
+#else
+extern "C" int hoa_debug_bounds(int extent_shift, int* status) {
+  if (status != nullptr) *status = 0;
+  (void)extent_shift;
+  return HOA_ERR_UNSUPPORTED;
+}
+#endif
+
 extern "C" int hoa_set_wait_bound(long long max_cycles) {
   if (max_cycles < 0 || max_cycles > sm100::kMaxWaitCycles) return HOA_ERR_INVALID_ARG;
   g_wait_bound.store(max_cycles == 0 ? sm100::kMaxWaitCycles : max_cycles, std::memory_order_relaxed);
@@ -557,6 +603,7 @@ extern "C" const char* hoa_status_string(int st) {
     case HOA_ERR_LAUNCH: return "CUDA launch failed";
     case HOA_ERR_WORKSPACE: return "workspace too small";
     case HOA_ERR_TIMEOUT: return "device-side wait timed out";
+    case HOA_ERR_BOUNDS: return "device-side index check failed (debug build)";
     default: return "unknown status";
   }
 }

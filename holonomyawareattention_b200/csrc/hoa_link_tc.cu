@@ -387,10 +387,17 @@ __global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, 1) link_tc_kernel(Link
                 x6 = kT8tc[5], x7 = kT8tc[6], y2 = kT8tc[7];
     const float c2 = y2 + x3 * x4;
 
+    const long long nrows = (long long)p.B * p.T * p.H;    // rows of a_all and of qkv
+    const long long BHT = nrows;                            // positions of R and U
     auto stage_gen = [&](int s) { return reinterpret_cast<float*>(stage_base + s * L::kStage); };
     auto stage_qkv = [&](int s) { return stage_base + s * L::kStage + L::kGenBytes; };
     auto fetch = [&](int s, int t) {        // thread 0: a_t and (q, k, v)_t into stage s
       const long long row = ((long long)b * p.T + t) * p.H + h;
+      // (debug build) a source row outside its buffer: no copy, the barrier completes empty
+      if (!(HOA_IN(row * m, m, nrows * m) && HOA_IN(row * kQkvBytes, kQkvBytes, nrows * kQkvBytes))) {
+        mbar_arrive_expect_tx(&bar_a[s], 0u);
+        return;
+      }
       mbar_arrive_expect_tx(&bar_a[s], (uint32_t)(m * 4 + kQkvBytes));
       bulk_load(stage_gen(s), p.a + row * m, m * 4, &bar_a[s]);
       bulk_load(stage_qkv(s), static_cast<const uint8_t*>(p.qkv) + row * (long long)kQkvBytes,
@@ -570,11 +577,12 @@ __global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, 1) link_tc_kernel(Link
     {
       const long long pos = (long long)chain * p.T + t0;
       float* Rg = p.R + pos * DP * DP;
-      for (int i = tid; i < DP * DP; i += NT) Rg[i] = (i / DP == i % DP) ? 1.f : 0.f;
-      float* Ug = p.U + pos * 3 * DP;
+      if (HOA_IN(pos * DP * DP, DP * DP, BHT * DP * DP))
+        for (int i = tid; i < DP * DP; i += NT) Rg[i] = (i / DP == i % DP) ? 1.f : 0.f;
+      float* Ug = HOA_IN(pos * 3 * DP, 3 * DP, BHT * 3 * DP) ? p.U + pos * 3 * DP : nullptr;
       const uint8_t* qv = stage_qkv(0);
       for (int i = tid; i < 3 * DP; i += NT)
-        Ug[i] = QB16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(qv)[i])
+        if (Ug != nullptr) Ug[i] = QB16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(qv)[i])
                      : reinterpret_cast<const float*>(qv)[i];
 #pragma unroll
       for (int j = 0; j < NCH; ++j) {
@@ -650,7 +658,8 @@ __global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, 1) link_tc_kernel(Link
       // ---- while P2 runs: R_t and U_t to global (t > t0; R_t^T row r is in TMEM)
       if (t > t0) {
         const long long pos = (long long)chain * p.T + t;
-        float* Rg = p.R + pos * DP * DP;
+        // (debug build) R_t outside its buffer: not written
+        float* Rg = HOA_IN(pos * DP * DP, DP * DP, BHT * DP * DP) ? p.R + pos * DP * DP : nullptr;
         const uint8_t* qv = stage_qkv(sidx);
         float u0 = 0.f, u1 = 0.f, u2 = 0.f;
 #pragma unroll
@@ -668,7 +677,7 @@ __global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, 1) link_tc_kernel(Link
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             const float v = rh[0][i] + rl[0][i];        // R_t[k][r], k = c0 + 8j + i
-            if (row_ok) Rg[(long long)(c0 + 8 * j + i) * DP + r] = v;
+            if (row_ok && Rg != nullptr) Rg[(long long)(c0 + 8 * j + i) * DP + r] = v;
             u0 = fmaf(v, qa[i], u0);
             u1 = fmaf(v, ka[i], u1);
             u2 = fmaf(v, va[i], u2);
@@ -702,10 +711,13 @@ __global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, 1) link_tc_kernel(Link
           s1 += sU[(qq * 3 + 1) * 128 + r];
           s2 += sU[(qq * 3 + 2) * 128 + r];
         }
-        float* Ug = p.U + ((long long)chain * p.T + t) * 3 * DP;
-        Ug[r] = s0;
-        Ug[DP + r] = s1;
-        Ug[2 * DP + r] = s2;
+        const long long upos = ((long long)chain * p.T + t) * 3 * DP;
+        if (HOA_IN(upos, 3 * DP, BHT * 3 * DP)) {
+          float* Ug = p.U + upos;
+          Ug[r] = s0;
+          Ug[DP + r] = s1;
+          Ug[2 * DP + r] = s2;
+        }
       }
       // stage sidx is free: position t + 2 (no new copy once a wait has given up:
       // the stage may still hold a copy in flight, which the drain waits for)
@@ -819,6 +831,8 @@ __global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, 1) link_tc_kernel(Link
       //      or the chunk total after the chunk's last edge
       wait_done(done_p4, ph_p4);
       {
+        const bool m_ok = HOA_IN(((long long)chain * p.K + kc) * DP * DP, DP * DP,
+                                 (long long)p.B * p.H * p.K * DP * DP);
         float* Mg = p.M + ((long long)chain * p.K + kc) * DP * DP;
 #pragma unroll
         for (int j = 0; j < NCH; ++j) {
@@ -835,7 +849,7 @@ __global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, 1) link_tc_kernel(Link
             const float v = (rh[i] + rl[i]) + dv[i];
             rh[i] = to_tf32(v);
             rl[i] = v - rh[i];
-            if (last && row_ok) Mg[(long long)(c0 + 8 * j + i) * DP + r] = v;
+            if (last && row_ok && m_ok) Mg[(long long)(c0 + 8 * j + i) * DP + r] = v;
           }
           tmem_st8(cRhi + lane + c0 + 8 * j, rh);
           tmem_st8(cRlo + lane + c0 + 8 * j, rl);

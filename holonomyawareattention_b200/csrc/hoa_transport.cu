@@ -101,7 +101,7 @@ constexpr int kXPos = 128;
 __global__ void __launch_bounds__(kXWarps * 32)
 out_transport_kernel(const float* __restrict__ o, const float* __restrict__ R,
                      const float* __restrict__ C, int chunk, int K, int nsub, void* out, int out_dtype,
-                     int H, int T, int d) {
+                     int BH, int H, int T, int d) {
   extern __shared__ __align__(16) float smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ld = d + 1;
@@ -115,11 +115,17 @@ out_transport_kernel(const float* __restrict__ o, const float* __restrict__ R,
   const int t_end = min(min(t_begin + kXPos, (kc + 1) * chunk), T);
   if (t_begin >= t_end) return;                   // block-uniform
   const float* Cg = C + ((long long)chain * K + kc) * d * d;
-  for (int i = threadIdx.x; i < d * d; i += blockDim.x) Cs[(i / d) * ld + i % d] = Cg[i];
+  const bool c_ok = HOA_IN(((long long)chain * K + kc) * d * d, d * d, (long long)BH * K * d * d);
+  for (int i = threadIdx.x; i < d * d; i += blockDim.x) Cs[(i / d) * ld + i % d] = c_ok ? Cg[i] : 0.f;
   __syncthreads();
   const int b = (int)(chain / H), h = (int)(chain % H);
   for (int t = t_begin + warp; t < t_end; t += kXWarps) {
     const long long pos = chain * T + t;
+    const long long obase = (((long long)b * T + t) * H + h) * d;
+    // (debug build) o_t, R_t and out_t inside their buffers; the position is skipped if not
+    if (!(HOA_IN(pos * d, d, (long long)BH * T * d) && HOA_IN(pos * d * d, d * d, (long long)BH * T * d * d) &&
+          HOA_IN(obase, d, (long long)BH * T * d)))
+      continue;                                   // warp-uniform
     for (int e = lane; e < d; e += 32) xo[e] = o[pos * d + e];
     __syncwarp();
     for (int e = lane; e < d; e += 32) {          // w = C_k o_t (rows of C_k from shared memory)
@@ -132,7 +138,6 @@ out_transport_kernel(const float* __restrict__ o, const float* __restrict__ R,
     if (d == 96) warp_matvec_fixed<96>(R + pos * d * d, w, xo, lane);
     else if (d == 64) warp_matvec_fixed<64>(R + pos * d * d, w, xo, lane);
     else warp_matvec(R + pos * d * d, w, xo, d, lane);
-    const long long obase = (((long long)b * T + t) * H + h) * d;
     for (int e = lane; e < d; e += 32) store_elem(out, obase + e, out_dtype, xo[e]);
     __syncwarp();
   }
@@ -159,6 +164,6 @@ extern "C" int hoa_out_transport(const float* o, const float* R, const float* C,
           cudaSuccess)
     return HOA_ERR_LAUNCH;
   out_transport_kernel<<<(unsigned)blocks, kXWarps * 32, smem, s>>>(
-      o, R, C, chunk, K, nsub, out, out_dtype, H, T, d);
+      o, R, C, chunk, K, nsub, out, out_dtype, B * H, H, T, d);
   return launch_status();
 }

@@ -51,7 +51,8 @@ typedef enum {
   HOA_ERR_UNSUPPORTED = 2,   /* head dim or dtype outside the compiled set  */
   HOA_ERR_LAUNCH = 3,        /* CUDA launch failed (cudaGetLastError)       */
   HOA_ERR_WORKSPACE = 4,     /* workspace too small                          */
-  HOA_ERR_TIMEOUT = 5        /* a bounded device-side wait gave up           */
+  HOA_ERR_TIMEOUT = 5,       /* a bounded device-side wait gave up           */
+  HOA_ERR_BOUNDS = 6         /* debug build: a device-side index check failed */
 } hoa_status;
 
 typedef enum { HOA_F32 = 0, HOA_BF16 = 1 } hoa_dtype;
@@ -287,6 +288,25 @@ int hoa_noalloc_status_word(int** dev_status);
  * report HOA_ERR_TIMEOUT in their status word; the output is not valid.
  */
 int hoa_set_wait_bound(long long max_cycles);
+
+/*
+ * hoa_debug_bounds — no counterpart in the reference.  Device-side index
+ * checks of the debug build (libhoa_debug.so, built with -DHOA_DEBUG_BOUNDS;
+ * compute-sanitizer is not available where this library is tested).  In that
+ * build every kernel of the core path checks, before each global access, that
+ * the element range a unit (a position, a chunk, a row) touches lies inside
+ * the extent its buffer has for the launch's shape; a check that fails
+ * records HOA_ERR_BOUNDS and the access is skipped (never performed; a
+ * skipped TMA copy completes its barrier with zero bytes), so nothing faults
+ * or traps.  The call returns in *status (host int) the first code recorded
+ * since the previous call on this device (0 if none) and clears it, after
+ * waiting for the device to finish; it then sets every check to compare
+ * against extents shifted right by `extent_shift` (0 = the true extents; a
+ * test hook: 1 makes the checks treat every buffer as half as long, so they
+ * fire on accesses that are really in bounds).  The product build returns
+ * HOA_ERR_UNSUPPORTED.
+ */
+int hoa_debug_bounds(int extent_shift, int* status);
 
 /*
  * hoa_edge_gemm — the second layer of the edge MLP (core/attention_fast_chunked.py:76,

@@ -33,6 +33,22 @@ def test_header_symbols_exported(lib):
         assert s in _lib.SIGNATURES, f"{s} has no ctypes signature"
 
 
+def test_debug_library_exports_the_same_abi():
+    """libhoa_debug.so (device-side index checks compiled in) exports every entry point too;
+    the product library answers hoa_debug_bounds with HOA_ERR_UNSUPPORTED (no GPU touched)."""
+    from holonomyawareattention_b200 import _build
+    _build.build(debug_bounds=True)
+    dbg = _lib.load_debug()
+    for s in declared_symbols():
+        assert hasattr(dbg, s), f"{s} missing from libhoa_debug.so"
+    st = ctypes.c_int(7)
+    assert _lib.load().hoa_debug_bounds(0, ctypes.byref(st)) == _lib.HOA_ERR_UNSUPPORTED
+    assert st.value == 0
+    assert dbg.hoa_debug_bounds(-1, ctypes.byref(st)) == _lib.HOA_ERR_INVALID_ARG
+    assert dbg.hoa_debug_bounds(0, None) == _lib.HOA_ERR_INVALID_ARG
+    assert b"index" in dbg.hoa_status_string(_lib.HOA_ERR_BOUNDS)
+
+
 def test_library_facts(lib):
     assert lib.hoa_abi_version() == 2
     assert lib.hoa_max_head_dim() == 120
