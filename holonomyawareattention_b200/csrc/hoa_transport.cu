@@ -115,17 +115,22 @@ out_transport_kernel(const float* __restrict__ o, const float* __restrict__ R,
   const int t_end = min(min(t_begin + kXPos, (kc + 1) * chunk), T);
   if (t_begin >= t_end) return;                   // block-uniform
   const float* Cg = C + ((long long)chain * K + kc) * d * d;
+#ifdef HOA_DEBUG_BOUNDS
   const bool c_ok = HOA_IN(((long long)chain * K + kc) * d * d, d * d, (long long)BH * K * d * d);
   for (int i = threadIdx.x; i < d * d; i += blockDim.x) Cs[(i / d) * ld + i % d] = c_ok ? Cg[i] : 0.f;
+#else
+  for (int i = threadIdx.x; i < d * d; i += blockDim.x) Cs[(i / d) * ld + i % d] = Cg[i];
+#endif
   __syncthreads();
   const int b = (int)(chain / H), h = (int)(chain % H);
   for (int t = t_begin + warp; t < t_end; t += kXWarps) {
     const long long pos = chain * T + t;
-    const long long obase = (((long long)b * T + t) * H + h) * d;
-    // (debug build) o_t, R_t and out_t inside their buffers; the position is skipped if not
+#ifdef HOA_DEBUG_BOUNDS
+    // o_t, R_t and out_t inside their buffers; the position is skipped if not (warp-uniform)
     if (!(HOA_IN(pos * d, d, (long long)BH * T * d) && HOA_IN(pos * d * d, d * d, (long long)BH * T * d * d) &&
-          HOA_IN(obase, d, (long long)BH * T * d)))
-      continue;                                   // warp-uniform
+          HOA_IN((((long long)b * T + t) * H + h) * d, d, (long long)BH * T * d)))
+      continue;
+#endif
     for (int e = lane; e < d; e += 32) xo[e] = o[pos * d + e];
     __syncwarp();
     for (int e = lane; e < d; e += 32) {          // w = C_k o_t (rows of C_k from shared memory)
@@ -138,6 +143,7 @@ out_transport_kernel(const float* __restrict__ o, const float* __restrict__ R,
     if (d == 96) warp_matvec_fixed<96>(R + pos * d * d, w, xo, lane);
     else if (d == 64) warp_matvec_fixed<64>(R + pos * d * d, w, xo, lane);
     else warp_matvec(R + pos * d * d, w, xo, d, lane);
+    const long long obase = (((long long)b * T + t) * H + h) * d;
     for (int e = lane; e < d; e += 32) store_elem(out, obase + e, out_dtype, xo[e]);
     __syncwarp();
   }
