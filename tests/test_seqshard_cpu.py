@@ -31,6 +31,17 @@ def _exclusive_products(M):            # (BH, N, d, d) -> exclusive products, fl
     return out
 
 
+def _by_value(*ts):
+    """numpy copies for the result queue: a tensor put on a torch multiprocessing queue is
+    shared through a file descriptor of the sending process, which may have exited by the
+    time the parent reads it."""
+    return tuple(t.detach().cpu().numpy().copy() for t in ts)
+
+
+def _received(vals):
+    return [torch.from_numpy(v) for v in vals]
+
+
 def _worker(rank, world, port, q):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -50,7 +61,7 @@ def _worker(rank, world, port, q):
         vt = torch.zeros(BH, d, ops.vt_stride(S), dtype=kh.dtype)
         vt[:, :, :S] = kh[:, s0:s1].transpose(1, 2)
         _, vt_all = seqshard.gather_kv(kh[:, s0:s1], vt, S, True, None)
-        q.put((rank, nxt, carry, k_all, v_all, vt_all))
+        q.put((rank, *_by_value(nxt, carry, k_all, v_all, vt_all)))
     finally:
         dist.destroy_process_group()
 
@@ -66,7 +77,7 @@ def test_sequence_shard_collectives(world):
     res = {}
     for _ in range(world):
         r, *vals = q.get(timeout=120)
-        res[r] = vals
+        res[r] = _received(vals)
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
@@ -124,7 +135,7 @@ def _seg_worker(rank, world, port, q, layout):
         v_loc = torch.stack([kh[:, s * S:(s + 1) * S].transpose(1, 2) for s in segs])
         k_all, v_all = seqshard.gather_kv_segments(k_loc, k_loc, S, False, layout, None)
         _, vt_all = seqshard.gather_kv_segments(k_loc, v_loc, S, True, layout, None)
-        q.put((rank, halos, carries, k_all, v_all, vt_all))
+        q.put((rank, *_by_value(halos, carries, k_all, v_all, vt_all)))
     finally:
         dist.destroy_process_group()
 
@@ -141,7 +152,7 @@ def test_segment_collectives(world, layout):
     res = {}
     for _ in range(world):
         r, *vals = q.get(timeout=120)
-        res[r] = vals
+        res[r] = _received(vals)
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
