@@ -654,6 +654,7 @@ __global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, 1) link_tc_kernel(Link
         }
       }
       const float sa = ldexpf(1.f, -nsq);
+      named_sync(kNamed, NT);                             // (as after N below)
 
       // ---- while P2 runs: R_t and U_t to global (t > t0; R_t^T row r is in TMEM)
       if (t > t0) {
@@ -820,6 +821,12 @@ __global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, 1) link_tc_kernel(Link
           for (int j = 0; j < NCH; ++j) hand_over(&ops_main[j], lid);
         }
       }
+      // Every compute warp has handed N over before any starts on A(t+1): a product
+      // starts on a chunk only once all warps have handed it over, and three warps
+      // share each SM sub-partition, so a warp that runs ahead only takes issue slots
+      // from the ones P4 waits for (measured: -1.2% link time with the barrier after
+      // the P2 operands below).
+      named_sync(kNamed, NT);
 
       // ---- while P4 runs: A(t+1) -> cA and X, then P1(t+1) is queued
       if (!last) {
