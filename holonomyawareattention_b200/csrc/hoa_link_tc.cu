@@ -57,7 +57,12 @@ struct LtLayout {
   static constexpr int NCH = CW / 8;                   // 8-column chunks per thread
   static constexpr int NT = 128 * CQ;                  // compute threads
   static constexpr int NW = NT / 32;                   // compute warps
-  static constexpr int NTHREADS = NT + 32;             // + the MMA warp
+  // + the MMA warp.  At d = 96 lane group 3 holds only padding rows, so the fourth SM
+  // sub-partition (warps 3, 7, 11, 15) has spare issue slots: the block gets 16 warps and
+  // warp 15 issues the products (warps 12-14 only take part in the block-wide barriers),
+  // instead of sharing sub-partition 0 with three compute warps (link -2.6..-4.9%).
+  static constexpr int kMmaWarp = DP == 96 ? 15 : NW;
+  static constexpr int NTHREADS = DP == 96 ? 512 : NT + 32;
   static_assert(CW % 8 == 0, "column groups must be multiples of 8");
   static constexpr int NSLAB = (DP + 31) / 32;
   static constexpr int kSlab = DP * 128;               // DP rows of 128 bytes
@@ -245,7 +250,7 @@ HOA_DEVICE void load8(const uint8_t* base, int i0, float (&v)[8]) {
 }
 
 // Warp roles.  Compute warps 0 .. NW-1 own the rows (TMEM lanes) and do all
-// elementwise work; warp NW (one elected lane) only issues the products.
+// elementwise work; warp kMmaWarp (one elected lane) only issues the products.
 // Each product's operands are handed over through an mbarrier (one arrival per
 // compute warp) and its completion is signalled by tcgen05.commit, so the
 // issuing thread never stalls the elementwise work.  Per position t, with
@@ -318,7 +323,7 @@ __global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, 1) link_tc_kernel(Link
                  sYlo = smem_u32(Ylo);
   bool bad = false;
 
-  if (warp == NW) {
+  if (warp == L::kMmaWarp) {
     // ------------------------------------------------------------ MMA warp
     if (lid == 0) {
       uint32_t ph_main = 0, ph_p1 = 0;   // bit j: phase parity of barrier j of the set
@@ -375,7 +380,7 @@ __global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, 1) link_tc_kernel(Link
       bad |= !mbar_wait(done_fin, 0);
     }
     __syncwarp();
-  } else {
+  } else if (warp < NW) {
     // -------------------------------------------------------- compute warps
     const int g = warp & 3, q = warp >> 2;
     const int r = g * 32 + lid;                          // this thread's row
@@ -704,30 +709,6 @@ __global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, 1) link_tc_kernel(Link
         }
       }
       named_sync(kNamed, NT);
-      if (t > t0 && q == 0 && row_ok) {                   // U_t: sum the column groups
-        float s0 = 0.f, s1 = 0.f, s2 = 0.f;
-#pragma unroll
-        for (int qq = 0; qq < CQ; ++qq) {
-          s0 += sU[(qq * 3 + 0) * 128 + r];
-          s1 += sU[(qq * 3 + 1) * 128 + r];
-          s2 += sU[(qq * 3 + 2) * 128 + r];
-        }
-        const long long upos = ((long long)chain * p.T + t) * 3 * DP;
-        if (HOA_IN(upos, 3 * DP, BHT * 3 * DP)) {
-          float* Ug = p.U + upos;
-          Ug[r] = s0;
-          Ug[DP + r] = s1;
-          Ug[2 * DP + r] = s2;
-        }
-      }
-      // stage sidx is free: position t + 2 (no new copy once a wait has given up:
-      // the stage may still hold a copy in flight, which the drain waits for)
-      if (tid == 0 && t + 2 < t1 && !bad && *s_abort == 0) {
-        fence_proxy_async_smem();
-        fetch(sidx, t + 2);
-        pend |= 1u << sidx;
-      }
-
       float n0r[NCH][8];                                  // N0, kept until N is formed
       // ---- P3 operands: X = L rows, Y^T = F^T rows; N0 = As + c2 A2s + x4 A4 (registers).
       //      A4 comes from registers and A4^T from the scratch, not from Q: P3
@@ -762,6 +743,32 @@ __global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, 1) link_tc_kernel(Link
           hand_over(&ops_main[j], lid);
         }
         tmem_wait_st();
+      }
+
+      // ---- after the P3 hand-overs (off the path to P3, which waits for every warp's
+      //      chunks): U_t from the column groups' partial sums, and the stage refill
+      if (t > t0 && q == 0 && row_ok) {                   // U_t: sum the column groups
+        float s0 = 0.f, s1 = 0.f, s2 = 0.f;
+#pragma unroll
+        for (int qq = 0; qq < CQ; ++qq) {
+          s0 += sU[(qq * 3 + 0) * 128 + r];
+          s1 += sU[(qq * 3 + 1) * 128 + r];
+          s2 += sU[(qq * 3 + 2) * 128 + r];
+        }
+        const long long upos = ((long long)chain * p.T + t) * 3 * DP;
+        if (HOA_IN(upos, 3 * DP, BHT * 3 * DP)) {
+          float* Ug = p.U + upos;
+          Ug[r] = s0;
+          Ug[DP + r] = s1;
+          Ug[2 * DP + r] = s2;
+        }
+      }
+      // stage sidx is free: position t + 2 (no new copy once a wait has given up:
+      // the stage may still hold a copy in flight, which the drain waits for)
+      if (tid == 0 && t + 2 < t1 && !bad && *s_abort == 0) {
+        fence_proxy_async_smem();
+        fetch(sidx, t + 2);
+        pend |= 1u << sidx;
       }
 
       // ---- N = G - I = N0 + L F, then nsq squarings N <- 2N + N N; N rows -> Y
