@@ -610,9 +610,11 @@ extern "C" const char* hoa_status_string(int st) {
 
 // Link-kernel CTAs resident per SM: the tensor-core kernel (d in {32, 48, 64,
 // 96}) is bound by its TMEM columns (5 d, rounded up to a power of two, of
-// 512), the SIMT kernel by its shared-memory footprint.
+// 512) and, at d = 32, by its registers (LtLayout::kMinBlocks); the SIMT
+// kernel by its shared-memory footprint.
 static int link_ctas_per_sm(int d) {
-  if (d == 32 || d == 48 || d == 64 || d == 96) {
+  if (d == 32) return 1;     // TMEM would allow two; 2 x 544 threads do not fit the registers
+  if (d == 48 || d == 64 || d == 96) {
     const int cols = 5 * d <= 128 ? 128 : (5 * d <= 256 ? 256 : 512);
     return 512 / cols;
   }

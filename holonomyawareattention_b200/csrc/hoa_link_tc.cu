@@ -95,6 +95,11 @@ struct LtLayout {
   // Request enough shared memory that no more CTAs share an SM than its 512
   // TMEM columns can serve (an allocation would otherwise wait for a peer).
   static constexpr int kMaxCtas = 512 / kTmemCols;
+  // CTAs per SM the registers must leave room for: at d = 48 two CTAs share the SM's TMEM
+  // (256 columns each), which 2 x 288 threads fit only at <= 112 registers a thread
+  // (unbounded the compiler takes 168, and one CTA per SM); at d = 32 two would need
+  // <= 60 registers for 2 x 544 threads, so one CTA runs (hoa_plan_chunk models both).
+  static constexpr int kMinBlocks = DP == 48 ? 2 : 1;
   static constexpr int kMinAlloc = 233472 / (kMaxCtas + 1);
   static constexpr int kAlloc = (kBytes + 1024 > kMinAlloc) ? kBytes + 1024 : kMinAlloc;
   static_assert(kSlab % 1024 == 0, "slabs must stay 1024-aligned");
@@ -261,7 +266,7 @@ HOA_DEVICE void load8(const uint8_t* base, int i0, float (&v)[8]) {
 //   R_{t+1} = R_t + P4 into TMEM    with P1(t+1),
 //   R_{t+1}, U_{t+1} to global      with P2(t+1).
 template <int DP, bool QB16, bool BANKED>
-__global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, 1) link_tc_kernel(LinkTcArgs p) {
+__global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, LtLayout<DP>::kMinBlocks) link_tc_kernel(LinkTcArgs p) {
   using L = LtLayout<DP>;
   constexpr int NCH = L::NCH, CW = L::CW, CQ = L::CQ, NT = L::NT, NW = L::NW;
   static_assert(!BANKED || DP % 32 == 0, "the banked generator layout needs d % 32 == 0");

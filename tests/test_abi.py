@@ -68,7 +68,7 @@ def test_plan_chunk(lib, B, H, T, d, sms):
         assert c == T
         return
     per_sm = 512 // (128 if 5 * d <= 128 else (256 if 5 * d <= 256 else 512)) \
-        if d in (32, 48, 64, 96) else None
+        if d in (48, 64, 96) else (1 if d == 32 else None)
 
     def cost(chunk, slots):
         units = B * H * (-(-T // chunk))
