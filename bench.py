@@ -43,6 +43,9 @@ CONFIGS = {
     # one batch row of c3 (same T, so the same attention shape), ~5 GB on the device:
     # the case the full ncu captures run on
     "c3b1": (1, 4096, 1536, 16, "bf16"),
+    # one batch row of configs[3] (head dim 120, the SIMT link kernel): the case its ncu
+    # captures run on
+    "c4b1": (1, 2048, 2880, 24, "bf16"),
     # one sequence of T=65536 split across the ranks (sequence sharding)
     "c5": (1, 65536, 1536, 16, "bf16"),
 }

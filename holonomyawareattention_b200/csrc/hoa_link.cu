@@ -610,21 +610,13 @@ extern "C" const char* hoa_status_string(int st) {
 
 // Link-kernel CTAs resident per SM: the tensor-core kernel (d in {32, 48, 64,
 // 96}) is bound by its TMEM columns (5 d, rounded up to a power of two, of
-// 512) and, at d = 32, by its registers (LtLayout::kMinBlocks); on a device
-// the occupancy query caps the model, so that a kernel whose registers or
-// shared memory admit fewer CTAs than its TMEM is planned as it runs.  The
-// SIMT kernel is bound by its shared-memory footprint.
-namespace hoa {
-int link_tc_resident_ctas(int d);
-}
+// 512) and, at d = 32, by its registers (LtLayout::kMinBlocks); the SIMT
+// kernel by its shared-memory footprint.
 static int link_ctas_per_sm(int d) {
-  if (d == 32 || d == 48 || d == 64 || d == 96) {
-    // the model: TMEM columns, and at d = 32 the registers (2 x 544 threads do not fit)
+  if (d == 32) return 1;     // TMEM would allow two; 2 x 544 threads do not fit the registers
+  if (d == 48 || d == 64 || d == 96) {
     const int cols = 5 * d <= 128 ? 128 : (5 * d <= 256 ? 256 : 512);
-    const int model = d == 32 ? 1 : 512 / cols;
-    // with a device, what it really keeps resident (never more than the TMEM allows)
-    const int real = hoa::link_tc_resident_ctas(d);
-    return real >= 1 && real < model ? real : model;
+    return 512 / cols;
   }
   const int dp = padded_dim(d);
   const size_t smem = (size_t)(4 * dp * dp + 4 * dp) * sizeof(float);

@@ -937,39 +937,4 @@ int link_local_tc(const void* a_all, int a_dtype, const float* a_bias, float edg
   }
 }
 
-// CTAs of the tensor-core link kernel one SM of the current device keeps
-// resident (the variant the module runs: bf16 q/k/v, banked generators where
-// d % 32 == 0), or 0 when it cannot be queried (no device, or d not served).
-template <int DP, bool BANKED>
-int resident_ctas() {
-  using L = LtLayout<DP>;
-  if (cudaFuncSetAttribute(link_tc_kernel<DP, true, BANKED>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           L::kAlloc) != cudaSuccess) {
-    cudaGetLastError();
-    return 0;
-  }
-  int n = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, link_tc_kernel<DP, true, BANKED>, L::NTHREADS,
-                                                    L::kAlloc) != cudaSuccess) {
-    cudaGetLastError();
-    return 0;
-  }
-  return n;
-}
-
-int link_tc_resident_ctas(int d) {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) {
-    cudaGetLastError();
-    return 0;
-  }
-  switch (d) {
-    case 32: return resident_ctas<32, true>();
-    case 48: return resident_ctas<48, false>();
-    case 64: return resident_ctas<64, true>();
-    case 96: return resident_ctas<96, true>();
-    default: return 0;
-  }
-}
-
 }  // namespace hoa

@@ -223,28 +223,3 @@ def test_edge_gelu_split_matches_torch(rows, cols, split):
         assert torch.equal(out[:, cols:], (g - hi.float()).to(torch.bfloat16))
     else:
         assert out.shape == (rows, cols)
-
-
-def _model_chunk(B, H, T, d, sms):
-    """hoa_plan_chunk's rule with the TMEM-bound CTAs per SM of the link kernel."""
-    per_sm = 1 if d == 32 else 512 // (128 if 5 * d <= 128 else (256 if 5 * d <= 256 else 512))
-    slots = sms * per_sm
-    best_cost, best = None, T
-    for K in range(1, T // 16 + 1):
-        chunk = -(-T // K)
-        units = B * H * (-(-T // chunk))
-        cost = -(-units // slots) * (chunk + 2)
-        if best_cost is None or cost < best_cost:
-            best_cost, best = cost, chunk
-    return best
-
-
-@pytest.mark.parametrize("B,H,T,d", [(64, 4, 512, 48), (16, 16, 4096, 96), (4, 16, 4096, 96),
-                                     (1, 16, 65536, 96)])
-def test_link_occupancy_matches_the_planner_model(B, H, T, d):
-    """On a device the chunk planner caps its occupancy model (TMEM columns) by what the
-    tensor-core link kernel really keeps resident per SM (registers, shared memory).  At the
-    configs' head dims the two must agree: a kernel that grew past its register budget would
-    run fewer CTAs per SM than the chunks were planned for (configs[1] lost 24% that way)."""
-    sms = torch.cuda.get_device_properties(0).multi_processor_count
-    assert ops.plan_chunk(B, H, T, d) == _model_chunk(B, H, T, d, sms)
