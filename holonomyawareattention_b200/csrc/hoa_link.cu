@@ -331,6 +331,337 @@ __global__ void __launch_bounds__(LinkCfg<DP>::NT, 1) link_local_kernel(LinkArgs
     for (int i = tid; i < d * d; i += NT) Mg[i] = bufR[(i / d) * DP + (i % d)];
 }
 
+// ---------------------------------------------------------------------------
+// The same unit for DP = 120 with every operand row-major.  Thread (ty, tx) of
+// the 15 x 15 grid owns rows ty + 15 i (i < 8) and columns 4 tx + j, 60 + 4 tx + j
+// (j < 4) of every product.  A product reads its left operand as float4 runs
+// along k of the thread's eight rows (the three row offsets of a warp fall on
+// different banks) and its right operand as two float4 of row k (15 contiguous
+// float4 per warp), and every result is stored row-major, so no product needs a
+// transposed operand: 6 shared-memory wavefronts per k per warp and no
+// bank-conflicted transposed stores.  Each output element accumulates the same
+// terms in the same k order as link_local_kernel, so R, U and M agree with it
+// (up to the rounding of the column sums behind the squaring count).
+// ---------------------------------------------------------------------------
+template <int DP> struct LinkRm {
+  static constexpr int G = DP / 8;                      // 15: thread grid is G x G
+  static constexpr int HALF = DP / 2;                   // column offset of the second float4 run
+  static constexpr int ACTIVE = G * G;
+  static constexpr int NT = ((ACTIVE + 31) / 32) * 32;
+  static_assert(DP % 8 == 0 && HALF == 4 * G, "two runs of 4 G columns");
+};
+
+template <int DP>
+HOA_DEVICE void mm_rm(const float* __restrict__ X, const float* __restrict__ Y, int ty, int tx,
+                      float (&acc)[8][8]) {
+  constexpr int G = LinkRm<DP>::G, HALF = LinkRm<DP>::HALF;
+  const float* xr = X + ty * DP;
+  const float* yc = Y + 4 * tx;
+#pragma unroll 2
+  for (int k0 = 0; k0 < DP; k0 += 4) {
+    float4 xv[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) xv[i] = *reinterpret_cast<const float4*>(xr + i * G * DP + k0);
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      const float4 y0 = *reinterpret_cast<const float4*>(yc + (k0 + kk) * DP);
+      const float4 y1 = *reinterpret_cast<const float4*>(yc + (k0 + kk) * DP + HALF);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float x = kk == 0 ? xv[i].x : (kk == 1 ? xv[i].y : (kk == 2 ? xv[i].z : xv[i].w));
+        acc[i][0] = fmaf(x, y0.x, acc[i][0]);
+        acc[i][1] = fmaf(x, y0.y, acc[i][1]);
+        acc[i][2] = fmaf(x, y0.z, acc[i][2]);
+        acc[i][3] = fmaf(x, y0.w, acc[i][3]);
+        acc[i][4] = fmaf(x, y1.x, acc[i][4]);
+        acc[i][5] = fmaf(x, y1.y, acc[i][5]);
+        acc[i][6] = fmaf(x, y1.z, acc[i][6]);
+        acc[i][7] = fmaf(x, y1.w, acc[i][7]);
+      }
+    }
+  }
+}
+
+// Offset of the thread's element (i, h) (h: column run 0 / 1) in a row-major DP x DP matrix.
+template <int DP>
+HOA_DEVICE int rm_off(int ty, int tx, int i, int h) {
+  return (ty + i * LinkRm<DP>::G) * DP + 4 * tx + h * LinkRm<DP>::HALF;
+}
+
+template <int DP>
+HOA_DEVICE void st_rm(float* __restrict__ Z, int ty, int tx, const float (&acc)[8][8]) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+      *reinterpret_cast<float4*>(Z + rm_off<DP>(ty, tx, i, h)) =
+          make_float4(acc[i][4 * h], acc[i][4 * h + 1], acc[i][4 * h + 2], acc[i][4 * h + 3]);
+}
+
+template <int DP>
+HOA_DEVICE float4 ld_rm(const float* __restrict__ Z, int ty, int tx, int i, int h) {
+  return *reinterpret_cast<const float4*>(Z + rm_off<DP>(ty, tx, i, h));
+}
+
+HOA_DEVICE float f4_at(const float4& v, int c) {
+  return c == 0 ? v.x : (c == 1 ? v.y : (c == 2 ? v.z : v.w));
+}
+
+// Element e of row pair q of the strict upper triangle of a d x d matrix: the
+// pair is row q followed by row d - 2 - q (d - 1 - q and q + 1 elements, d in all;
+// for even d the middle row q = d/2 - 1 stands alone).  Returns false past the
+// pair's end or past the last pair (q >= d/2); m = d (d - 1) / 2 elements in all.
+HOA_DEVICE bool pair_elem(int q, int e, int d, int& row, int& col) {
+  const int len1 = d - 1 - q;
+  const int q2 = d - 2 - q;
+  const int len = q2 == q ? len1 : d;
+  const bool first = e < len1;
+  row = first ? q : q2;
+  col = row + 1 + (first ? e : e - len1);
+  return q < d / 2 && e < len;
+}
+
+template <int DP>
+__global__ void __launch_bounds__(LinkRm<DP>::NT, 1) link_local_rm_kernel(LinkArgs p) {
+  using C = LinkCfg<DP>;
+  using Rm = LinkRm<DP>;
+  constexpr int NT = Rm::NT, G = Rm::G, HALF = Rm::HALF;
+  extern __shared__ __align__(16) float smem[];
+  float* bufR = smem;              // running local product R
+  float* bufA = bufR + C::MAT;     // A, later G
+  float* buf1 = bufA + C::MAT;     // A2s, later L
+  float* buf2 = buf1 + C::MAT;     // T1, later the right factor Rf of A8
+  float* svec = buf2 + C::MAT;     // q, k, v of the current position (3*DP)
+  float* colsum = svec + 3 * DP;   // column abs-sums of A2 (DP)
+  __shared__ int s_squarings;
+
+  const int tid = threadIdx.x;
+  const int chain = blockIdx.x / p.K;
+  const int kc = blockIdx.x % p.K;
+  const int b = chain / p.H, h = chain % p.H;
+  const int d = p.d;
+  const int m = d * (d - 1) / 2;
+  const int t0 = kc * p.chunk;
+  const int t1 = min(t0 + p.chunk, p.T);
+  const bool active = tid < Rm::ACTIVE;
+  const int ty = tid / G, tx = tid % G;
+  // R_t leaves as float4 rows when it has no padding and R is 16-byte aligned
+  const bool r_vec = d == DP && (reinterpret_cast<uintptr_t>(p.R) & 15) == 0;
+  constexpr int NW = NT / 32;
+  const int warp = tid >> 5, lane = tid & 31;
+  constexpr int kPairsPerWarp = (DP / 2 + NW - 1) / NW;         // row pairs per warp (d/2 pairs)
+  constexpr int kPairChunks = (DP + 31) / 32;                   // a pair holds d <= DP elements
+  constexpr int kVecPer = (3 * DP + NT - 1) / NT;               // q, k, v elements per thread
+
+  for (int i = tid; i < C::MAT; i += NT) bufR[i] = (i / DP == i % DP) ? 1.f : 0.f;
+  __syncthreads();
+
+  float acc[8][8];
+  float E[8][8];
+  const long long BH = (long long)p.B * p.H;
+  for (int t = t0; t < t1; ++t) {
+    // ---- position t: R_t and the locally transported q, k, v -------------
+    const long long pos = (long long)chain * p.T + t;
+    const long long qbase = (((long long)b * p.T + t) * p.H + h) * 3LL * d;
+    const long long abase = (((long long)b * p.T + t) * p.H + h) * (long long)p.a_stride;
+    // (debug build) every buffer range of this position; a failed one is skipped
+    const bool r_ok = HOA_IN(pos * d * d, d * d, BH * p.T * d * d);
+    const bool q_ok = HOA_IN(qbase, 3 * d, BH * p.T * 3 * d);
+    const bool a_ok = HOA_IN(abase, p.a_stride, BH * p.T * p.a_stride);
+    const bool u_ok = HOA_IN(pos * 3 * d, 3 * d, BH * p.T * 3 * d);
+    // ---- this position's inputs: every load is issued before any is used -----
+    // The generator row a_t in row pairs: warp w takes pairs q = w, w + NW, ... of
+    // rows q and d - 2 - q of the strict upper triangle (d elements together; the
+    // middle row of an even d alone), lane l their elements l, l + 32, ...
+    // (the element indices do not change with t; an opaque copy of d keeps the
+    // compiler from holding all of them in registers across the position loop)
+    int dl;
+    asm volatile("mov.b32 %0, %1;" : "=r"(dl) : "r"(d));
+    float gv[kPairsPerWarp][kPairChunks];
+#pragma unroll
+    for (int u = 0; u < kPairsPerWarp; ++u)
+#pragma unroll
+      for (int c = 0; c < kPairChunks; ++c) {
+        int row, col;
+        const bool ok = pair_elem(warp + u * NW, lane + 32 * c, dl, row, col);
+        const int idx = row * (2 * dl - row - 1) / 2 + col - row - 1;
+        const int slot = p.a_banked ? gen_banked_slot(row, col, dl) : idx;
+        gv[u][c] = (ok && a_ok) ? load_elem(p.a, abase + slot, p.a_dtype) : 0.f;
+      }
+    float qv[kVecPer];
+#pragma unroll
+    for (int u = 0; u < kVecPer; ++u) {
+      const int i = tid + u * NT, v = i / DP, e = i % DP;
+      qv[u] = (i < 3 * DP && e < d && q_ok) ? load_elem(p.qkv, qbase + (long long)v * d + e, p.qkv_dtype) : 0.f;
+    }
+    float* Rg = p.R + pos * d * d;
+    if (r_ok) {
+      if (r_vec) {
+        for (int i = tid; i < DP * DP / 4; i += NT)
+          reinterpret_cast<float4*>(Rg)[i] = reinterpret_cast<const float4*>(bufR)[i];
+      } else {
+        for (int i = tid; i < d * d; i += NT) Rg[i] = bufR[(i / d) * DP + (i % d)];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kVecPer; ++u)
+      if (tid + u * NT < 3 * DP) svec[tid + u * NT] = qv[u];
+    // ---- edge t: A = skew(edge_scale * a_t) ------------------------------
+#pragma unroll
+    for (int u = 0; u < kPairsPerWarp; ++u)
+#pragma unroll
+      for (int c = 0; c < kPairChunks; ++c) {
+        int row, col;
+        if (pair_elem(warp + u * NW, lane + 32 * c, dl, row, col)) {
+          float av = gv[u][c];
+          if (p.a_bias != nullptr) {
+            const int idx = row * (2 * dl - row - 1) / 2 + col - row - 1;
+            av += p.a_bias[(long long)h * p.a_stride + (p.a_banked ? gen_banked_slot(row, col, dl) : idx)];
+          }
+          const float v = __fmul_rn(av, p.edge_scale);
+          bufA[row * DP + col] = v;
+          bufA[col * DP + row] = -v;
+        }
+      }
+    for (int i = tid; i < DP; i += NT) { bufA[i * DP + i] = 0.f; colsum[i] = 0.f; }
+    if (d < DP) {
+      for (int i = tid; i < DP * (DP - d); i += NT) {
+        const int r = i / (DP - d), c = d + i % (DP - d);
+        bufA[r * DP + c] = 0.f;
+        bufA[c * DP + r] = 0.f;
+      }
+    }
+    __syncthreads();
+    // U_t = R_t^T [q, k, v]: thread e < DP sums column e of R against all three
+    // (over the padded width: R's padding rows and the vectors' padding are 0)
+    float* Ug = p.U + pos * 3 * d;
+    if (tid < DP) {
+      float s0 = 0.f, s1 = 0.f, s2 = 0.f;
+#pragma unroll 8
+      for (int r = 0; r < DP; ++r) {
+        const float x = bufR[r * DP + tid];
+        s0 = fmaf(x, svec[r], s0);
+        s1 = fmaf(x, svec[DP + r], s1);
+        s2 = fmaf(x, svec[2 * DP + r], s2);
+      }
+      if (tid < d && u_ok) {
+        Ug[tid] = s0;
+        Ug[d + tid] = s1;
+        Ug[2 * d + tid] = s2;
+      }
+    }
+
+    // ---- A2 = A A; theta^2 = ||A2||_1 ---------------------------------------
+    zero_acc(acc);
+    if (active) {
+      mm_rm<DP>(bufA, bufA, ty, tx, acc);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float cs = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) cs += fabsf(acc[i][j]);
+        atomicAdd(&colsum[4 * tx + (j & 3) + (j >> 2) * HALF], cs);
+      }
+    }
+    __syncthreads();
+    if (tid < 32) {
+      float mx = 0.f;
+      for (int c = tid; c < DP; c += 32) mx = fmaxf(mx, colsum[c]);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      if (tid == 0) {
+        float theta = sqrtf(mx);
+        int s = 0;
+        while (theta > kTheta8 && s < 64) { theta *= 0.5f; ++s; }
+        s_squarings = s;
+      }
+    }
+    __syncthreads();
+    const int nsq = s_squarings;
+    const float sa = ldexpf(1.f, -nsq), sa2 = ldexpf(1.f, -2 * nsq);
+    const float x1 = kT8[0], x2 = kT8[1], x3 = kT8[2], x4 = kT8[3], x5 = kT8[4], x6 = kT8[5],
+                x7 = kT8[6], y2 = kT8[7];
+
+    // ---- A2s -> buf1, T1 = x1 As + x2 A2s -> buf2 ---------------------------
+    if (active) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const float4 av = ld_rm<DP>(bufA, ty, tx, i, hh);
+          float a2[4], t1v[4];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            a2[c] = acc[i][4 * hh + c] * sa2;
+            t1v[c] = x1 * (f4_at(av, c) * sa) + x2 * a2[c];
+          }
+          const int o = rm_off<DP>(ty, tx, i, hh);
+          *reinterpret_cast<float4*>(buf1 + o) = make_float4(a2[0], a2[1], a2[2], a2[3]);
+          *reinterpret_cast<float4*>(buf2 + o) = make_float4(t1v[0], t1v[1], t1v[2], t1v[3]);
+        }
+    }
+    __syncthreads();
+
+    // ---- A4 = A2s T1 ------------------------------------------------------------
+    zero_acc(acc);
+    if (active) mm_rm<DP>(buf1, buf2, ty, tx, acc);
+    __syncthreads();
+    if (active) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const float4 av = ld_rm<DP>(bufA, ty, tx, i, hh);
+          const float4 a2v = ld_rm<DP>(buf1, ty, tx, i, hh);
+          const int r = ty + i * G;
+          float rf[4];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const int col = 4 * tx + hh * HALF + c;
+            const float a = f4_at(av, c) * sa, a2 = f4_at(a2v, c), a4 = acc[i][4 * hh + c];
+            const float id = (r == col) ? 1.f : 0.f;
+            rf[c] = x4 * id + x5 * a + x6 * a2 + x7 * a4;       // right factor
+            E[i][4 * hh + c] = id + a + y2 * a2;                // I + A + y2 A2
+            acc[i][4 * hh + c] = x3 * a2 + a4;                  // left factor L
+          }
+          *reinterpret_cast<float4*>(buf2 + rm_off<DP>(ty, tx, i, hh)) = make_float4(rf[0], rf[1], rf[2], rf[3]);
+        }
+    }
+    __syncthreads();
+    if (active) st_rm<DP>(buf1, ty, tx, acc);                    // L
+    __syncthreads();
+
+    // ---- G = E + L Rf; then s squarings G <- G G --------------------------------
+    if (active) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = E[i][j];
+      mm_rm<DP>(buf1, buf2, ty, tx, acc);
+      st_rm<DP>(bufA, ty, tx, acc);                              // G
+    }
+    for (int sq = 0; sq < nsq; ++sq) {
+      __syncthreads();
+      zero_acc(acc);
+      if (active) mm_rm<DP>(bufA, bufA, ty, tx, acc);
+      __syncthreads();
+      if (active) st_rm<DP>(bufA, ty, tx, acc);
+    }
+    __syncthreads();
+
+    // ---- R <- G R ----------------------------------------------------------
+    zero_acc(acc);
+    if (active) mm_rm<DP>(bufA, bufR, ty, tx, acc);
+    __syncthreads();
+    if (active) st_rm<DP>(bufR, ty, tx, acc);
+    __syncthreads();
+  }
+  // chunk total: R after the chunk's last edge
+  float* Mg = p.M + ((long long)chain * p.K + kc) * d * d;
+  if (HOA_IN(((long long)chain * p.K + kc) * d * d, d * d, BH * p.K * d * d))
+    for (int i = tid; i < d * d; i += NT) Mg[i] = bufR[(i / d) * DP + (i % d)];
+}
+
 // C_0 = carry_in (or I), C_{k+1} = M_k C_k.  One CTA per chain.
 template <int DP>
 __global__ void __launch_bounds__(LinkCfg<DP>::NT, 1)
@@ -514,11 +845,20 @@ int launch_carry_apply(const float* U, const float* C, void* qh, void* kh, void*
 template <int DP>
 int launch_link_local(const LinkArgs& a, cudaStream_t s) {
   using C = LinkCfg<DP>;
-  if (cudaFuncSetAttribute(link_local_kernel<DP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)C::kLinkSmem) != cudaSuccess)
+  // DP = 120 runs the row-major variant (same results, fewer shared-memory wavefronts)
+  void (*kern)(LinkArgs);
+  int nt;
+  if constexpr (DP == 120) {
+    kern = link_local_rm_kernel<DP>;
+    nt = LinkRm<DP>::NT;
+  } else {
+    kern = link_local_kernel<DP>;
+    nt = C::NT;
+  }
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kLinkSmem) != cudaSuccess)
     return HOA_ERR_LAUNCH;
   const long long units = (long long)a.B * a.H * a.K;
-  link_local_kernel<DP><<<(unsigned)units, C::NT, C::kLinkSmem, s>>>(a);
+  kern<<<(unsigned)units, nt, C::kLinkSmem, s>>>(a);
   return launch_status();
 }
 
