@@ -333,41 +333,42 @@ __global__ void __launch_bounds__(LinkCfg<DP>::NT, 1) link_local_kernel(LinkArgs
 
 // ---------------------------------------------------------------------------
 // The same unit for DP = 120 with every operand row-major.  Thread (ty, tx) of
-// the 15 x 15 grid owns rows ty + 15 i (i < 8) and columns 4 tx + j, 60 + 4 tx + j
-// (j < 4) of every product.  A product reads its left operand as float4 runs
-// along k of the thread's eight rows (the three row offsets of a warp fall on
-// different banks) and its right operand as two float4 of row k (15 contiguous
-// float4 per warp), and every result is stored row-major, so no product needs a
-// transposed operand: 6 shared-memory wavefronts per k per warp and no
-// bank-conflicted transposed stores.  Each output element accumulates the same
+// the GR x 15 grid owns rows ty + GR i (i < RI, GR = DP / RI) and columns
+// 4 tx + j, 60 + 4 tx + j (j < 4) of every product.  A product reads its left
+// operand as float4 runs along k of the thread's RI rows (the row offsets of a
+// warp fall on different banks) and its right operand as two float4 of row k
+// (15 contiguous float4 per warp), and every result is stored row-major, so no
+// product needs a transposed operand and no store is bank-conflicted.  Each output element accumulates the same
 // terms in the same k order as link_local_kernel, so R, U and M agree with it
 // (up to the rounding of the column sums behind the squaring count).
 // ---------------------------------------------------------------------------
 template <int DP> struct LinkRm {
-  static constexpr int G = DP / 8;                      // 15: thread grid is G x G
+  static constexpr int RI = 8;                          // rows per thread (8 x 8 tiles, 225 threads)
+  static constexpr int GR = DP / RI;                    // row groups (thread rows ty + GR i)
+  static constexpr int GC = DP / 8;                     // column groups: two runs of 4 columns
   static constexpr int HALF = DP / 2;                   // column offset of the second float4 run
-  static constexpr int ACTIVE = G * G;
+  static constexpr int ACTIVE = GR * GC;
   static constexpr int NT = ((ACTIVE + 31) / 32) * 32;
-  static_assert(DP % 8 == 0 && HALF == 4 * G, "two runs of 4 G columns");
+  static_assert(DP % 8 == 0 && DP % RI == 0 && HALF == 4 * GC, "two runs of 4 GC columns");
 };
 
 template <int DP>
 HOA_DEVICE void mm_rm(const float* __restrict__ X, const float* __restrict__ Y, int ty, int tx,
-                      float (&acc)[8][8]) {
-  constexpr int G = LinkRm<DP>::G, HALF = LinkRm<DP>::HALF;
+                      float (&acc)[LinkRm<DP>::RI][8]) {
+  constexpr int RI = LinkRm<DP>::RI, GR = LinkRm<DP>::GR, HALF = LinkRm<DP>::HALF;
   const float* xr = X + ty * DP;
   const float* yc = Y + 4 * tx;
 #pragma unroll 2
   for (int k0 = 0; k0 < DP; k0 += 4) {
-    float4 xv[8];
+    float4 xv[RI];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) xv[i] = *reinterpret_cast<const float4*>(xr + i * G * DP + k0);
+    for (int i = 0; i < RI; ++i) xv[i] = *reinterpret_cast<const float4*>(xr + i * GR * DP + k0);
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) {
       const float4 y0 = *reinterpret_cast<const float4*>(yc + (k0 + kk) * DP);
       const float4 y1 = *reinterpret_cast<const float4*>(yc + (k0 + kk) * DP + HALF);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
+      for (int i = 0; i < RI; ++i) {
         const float x = kk == 0 ? xv[i].x : (kk == 1 ? xv[i].y : (kk == 2 ? xv[i].z : xv[i].w));
         acc[i][0] = fmaf(x, y0.x, acc[i][0]);
         acc[i][1] = fmaf(x, y0.y, acc[i][1]);
@@ -385,13 +386,13 @@ HOA_DEVICE void mm_rm(const float* __restrict__ X, const float* __restrict__ Y, 
 // Offset of the thread's element (i, h) (h: column run 0 / 1) in a row-major DP x DP matrix.
 template <int DP>
 HOA_DEVICE int rm_off(int ty, int tx, int i, int h) {
-  return (ty + i * LinkRm<DP>::G) * DP + 4 * tx + h * LinkRm<DP>::HALF;
+  return (ty + i * LinkRm<DP>::GR) * DP + 4 * tx + h * LinkRm<DP>::HALF;
 }
 
 template <int DP>
-HOA_DEVICE void st_rm(float* __restrict__ Z, int ty, int tx, const float (&acc)[8][8]) {
+HOA_DEVICE void st_rm(float* __restrict__ Z, int ty, int tx, const float (&acc)[LinkRm<DP>::RI][8]) {
 #pragma unroll
-  for (int i = 0; i < 8; ++i)
+  for (int i = 0; i < LinkRm<DP>::RI; ++i)
 #pragma unroll
     for (int h = 0; h < 2; ++h)
       *reinterpret_cast<float4*>(Z + rm_off<DP>(ty, tx, i, h)) =
@@ -425,7 +426,7 @@ template <int DP>
 __global__ void __launch_bounds__(LinkRm<DP>::NT, 1) link_local_rm_kernel(LinkArgs p) {
   using C = LinkCfg<DP>;
   using Rm = LinkRm<DP>;
-  constexpr int NT = Rm::NT, G = Rm::G, HALF = Rm::HALF;
+  constexpr int NT = Rm::NT, RI = Rm::RI, GR = Rm::GR, HALF = Rm::HALF;
   extern __shared__ __align__(16) float smem[];
   float* bufR = smem;              // running local product R
   float* bufA = bufR + C::MAT;     // A, later G
@@ -444,7 +445,7 @@ __global__ void __launch_bounds__(LinkRm<DP>::NT, 1) link_local_rm_kernel(LinkAr
   const int t0 = kc * p.chunk;
   const int t1 = min(t0 + p.chunk, p.T);
   const bool active = tid < Rm::ACTIVE;
-  const int ty = tid / G, tx = tid % G;
+  const int ty = tid / Rm::GC, tx = tid % Rm::GC;
   // R_t leaves as float4 rows when it has no padding and R is 16-byte aligned
   const bool r_vec = d == DP && (reinterpret_cast<uintptr_t>(p.R) & 15) == 0;
   constexpr int NW = NT / 32;
@@ -456,8 +457,7 @@ __global__ void __launch_bounds__(LinkRm<DP>::NT, 1) link_local_rm_kernel(LinkAr
   for (int i = tid; i < C::MAT; i += NT) bufR[i] = (i / DP == i % DP) ? 1.f : 0.f;
   __syncthreads();
 
-  float acc[8][8];
-  float E[8][8];
+  float acc[RI][8];
   const long long BH = (long long)p.B * p.H;
   for (int t = t0; t < t1; ++t) {
     // ---- position t: R_t and the locally transported q, k, v -------------
@@ -551,110 +551,118 @@ __global__ void __launch_bounds__(LinkRm<DP>::NT, 1) link_local_rm_kernel(LinkAr
       }
     }
 
-    // ---- A2 = A A; theta^2 = ||A2||_1 ---------------------------------------
-    zero_acc(acc);
-    if (active) {
-      mm_rm<DP>(bufA, bufA, ty, tx, acc);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        float cs = 0.f;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) cs += fabsf(acc[i][j]);
-        atomicAdd(&colsum[4 * tx + (j & 3) + (j >> 2) * HALF], cs);
-      }
-    }
-    __syncthreads();
-    if (tid < 32) {
-      float mx = 0.f;
-      for (int c = tid; c < DP; c += 32) mx = fmaxf(mx, colsum[c]);
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      if (tid == 0) {
-        float theta = sqrtf(mx);
-        int s = 0;
-        while (theta > kTheta8 && s < 64) { theta *= 0.5f; ++s; }
-        s_squarings = s;
-      }
-    }
-    __syncthreads();
-    const int nsq = s_squarings;
-    const float sa = ldexpf(1.f, -nsq), sa2 = ldexpf(1.f, -2 * nsq);
+    // ---- the products ----------------------------------------------------------
+    // step kind 0: A2 = A A          1: A4 = A2s T1        2: G = E + L Rf
+    //           3: G <- G G (s times) 4: R <- G R
+    // One call site of mm_rm serves every product (a single copy of its unrolled
+    // loop in the instruction cache); E waits in bufA in place of A for step 2.
     const float x1 = kT8[0], x2 = kT8[1], x3 = kT8[2], x4 = kT8[3], x5 = kT8[4], x6 = kT8[5],
                 x7 = kT8[6], y2 = kT8[7];
-
-    // ---- A2s -> buf1, T1 = x1 As + x2 A2s -> buf2 ---------------------------
-    if (active) {
+    int nsq = 0;
+    float sa = 1.f, sa2 = 1.f;
+    for (int step = 0;; ++step) {
+      const int kind = step < 3 ? step : (step < 3 + nsq ? 3 : 4);
+      const float* X = (kind == 1 || kind == 2) ? buf1 : bufA;
+      const float* Y = (kind == 0 || kind == 3) ? bufA : (kind == 4 ? bufR : buf2);
+      if (active) {
+        if (kind == 2) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
+          for (int i = 0; i < RI; ++i)
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          const float4 av = ld_rm<DP>(bufA, ty, tx, i, hh);
-          float a2[4], t1v[4];
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            a2[c] = acc[i][4 * hh + c] * sa2;
-            t1v[c] = x1 * (f4_at(av, c) * sa) + x2 * a2[c];
-          }
-          const int o = rm_off<DP>(ty, tx, i, hh);
-          *reinterpret_cast<float4*>(buf1 + o) = make_float4(a2[0], a2[1], a2[2], a2[3]);
-          *reinterpret_cast<float4*>(buf2 + o) = make_float4(t1v[0], t1v[1], t1v[2], t1v[3]);
+            for (int hh = 0; hh < 2; ++hh) {
+              const float4 e = ld_rm<DP>(bufA, ty, tx, i, hh);
+              acc[i][4 * hh] = e.x; acc[i][4 * hh + 1] = e.y; acc[i][4 * hh + 2] = e.z; acc[i][4 * hh + 3] = e.w;
+            }
+        } else {
+          zero_acc(acc);
         }
-    }
-    __syncthreads();
-
-    // ---- A4 = A2s T1 ------------------------------------------------------------
-    zero_acc(acc);
-    if (active) mm_rm<DP>(buf1, buf2, ty, tx, acc);
-    __syncthreads();
-    if (active) {
+        mm_rm<DP>(X, Y, ty, tx, acc);
+      }
+      if (kind == 0) {
+        // theta^2 = ||A2||_1 -> the squaring count; then A2s -> buf1, T1 = x1 As + x2 A2s -> buf2
+        if (active) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
+          for (int j = 0; j < 8; ++j) {
+            float cs = 0.f;
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          const float4 av = ld_rm<DP>(bufA, ty, tx, i, hh);
-          const float4 a2v = ld_rm<DP>(buf1, ty, tx, i, hh);
-          const int r = ty + i * G;
-          float rf[4];
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const int col = 4 * tx + hh * HALF + c;
-            const float a = f4_at(av, c) * sa, a2 = f4_at(a2v, c), a4 = acc[i][4 * hh + c];
-            const float id = (r == col) ? 1.f : 0.f;
-            rf[c] = x4 * id + x5 * a + x6 * a2 + x7 * a4;       // right factor
-            E[i][4 * hh + c] = id + a + y2 * a2;                // I + A + y2 A2
-            acc[i][4 * hh + c] = x3 * a2 + a4;                  // left factor L
+            for (int i = 0; i < RI; ++i) cs += fabsf(acc[i][j]);
+            atomicAdd(&colsum[4 * tx + (j & 3) + (j >> 2) * HALF], cs);
           }
-          *reinterpret_cast<float4*>(buf2 + rm_off<DP>(ty, tx, i, hh)) = make_float4(rf[0], rf[1], rf[2], rf[3]);
         }
-    }
-    __syncthreads();
-    if (active) st_rm<DP>(buf1, ty, tx, acc);                    // L
-    __syncthreads();
-
-    // ---- G = E + L Rf; then s squarings G <- G G --------------------------------
-    if (active) {
+        __syncthreads();
+        if (tid < 32) {
+          float mx = 0.f;
+          for (int c = tid; c < DP; c += 32) mx = fmaxf(mx, colsum[c]);
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
+          for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+          if (tid == 0) {
+            float theta = sqrtf(mx);
+            int sc = 0;
+            while (theta > kTheta8 && sc < 64) { theta *= 0.5f; ++sc; }
+            s_squarings = sc;
+          }
+        }
+        __syncthreads();
+        nsq = s_squarings;
+        sa = ldexpf(1.f, -nsq);
+        sa2 = ldexpf(1.f, -2 * nsq);
+        if (active) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[i][j] = E[i][j];
-      mm_rm<DP>(buf1, buf2, ty, tx, acc);
-      st_rm<DP>(bufA, ty, tx, acc);                              // G
+          for (int i = 0; i < RI; ++i)
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+              const float4 av = ld_rm<DP>(bufA, ty, tx, i, hh);
+              float a2[4], t1v[4];
+#pragma unroll
+              for (int c = 0; c < 4; ++c) {
+                a2[c] = acc[i][4 * hh + c] * sa2;
+                t1v[c] = x1 * (f4_at(av, c) * sa) + x2 * a2[c];
+              }
+              const int o = rm_off<DP>(ty, tx, i, hh);
+              *reinterpret_cast<float4*>(buf1 + o) = make_float4(a2[0], a2[1], a2[2], a2[3]);
+              *reinterpret_cast<float4*>(buf2 + o) = make_float4(t1v[0], t1v[1], t1v[2], t1v[3]);
+            }
+        }
+        __syncthreads();
+      } else if (kind == 1) {
+        // Rf -> buf2, E = I + As + y2 A2s -> bufA, L = x3 A2s + A4 -> buf1
+        __syncthreads();
+        if (active) {
+#pragma unroll
+          for (int i = 0; i < RI; ++i)
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+              const float4 av = ld_rm<DP>(bufA, ty, tx, i, hh);
+              const float4 a2v = ld_rm<DP>(buf1, ty, tx, i, hh);
+              const int r = ty + i * GR;
+              float rf[4], ev[4];
+#pragma unroll
+              for (int c = 0; c < 4; ++c) {
+                const int col = 4 * tx + hh * HALF + c;
+                const float a = f4_at(av, c) * sa, a2 = f4_at(a2v, c), a4 = acc[i][4 * hh + c];
+                const float id = (r == col) ? 1.f : 0.f;
+                rf[c] = x4 * id + x5 * a + x6 * a2 + x7 * a4;   // right factor
+                ev[c] = id + a + y2 * a2;                       // I + A + y2 A2
+                acc[i][4 * hh + c] = x3 * a2 + a4;              // left factor L
+              }
+              const int o = rm_off<DP>(ty, tx, i, hh);
+              *reinterpret_cast<float4*>(buf2 + o) = make_float4(rf[0], rf[1], rf[2], rf[3]);
+              *reinterpret_cast<float4*>(bufA + o) = make_float4(ev[0], ev[1], ev[2], ev[3]);
+            }
+        }
+        __syncthreads();
+        if (active) st_rm<DP>(buf1, ty, tx, acc);
+        __syncthreads();
+      } else if (kind == 2) {
+        if (active) st_rm<DP>(bufA, ty, tx, acc);              // G (each thread its own E slots)
+        __syncthreads();
+      } else {
+        __syncthreads();
+        if (active) st_rm<DP>(kind == 3 ? bufA : bufR, ty, tx, acc);
+        __syncthreads();
+        if (kind == 4) break;
+      }
     }
-    for (int sq = 0; sq < nsq; ++sq) {
-      __syncthreads();
-      zero_acc(acc);
-      if (active) mm_rm<DP>(bufA, bufA, ty, tx, acc);
-      __syncthreads();
-      if (active) st_rm<DP>(bufA, ty, tx, acc);
-    }
-    __syncthreads();
-
-    // ---- R <- G R ----------------------------------------------------------
-    zero_acc(acc);
-    if (active) mm_rm<DP>(bufA, bufR, ty, tx, acc);
-    __syncthreads();
-    if (active) st_rm<DP>(bufR, ty, tx, acc);
-    __syncthreads();
   }
   // chunk total: R after the chunk's last edge
   float* Mg = p.M + ((long long)chain * p.K + kc) * d * d;
