@@ -78,15 +78,40 @@ class ClockSampler:
         self.proc = None
         self.path = None
 
+    def _rows(self):
+        rows = []
+        try:
+            with open(self.path) as f:
+                for line in f:
+                    parts = [s.strip() for s in line.split(",")]
+                    if len(parts) >= 9:
+                        rows.append(parts)
+        except OSError:
+            pass
+        return rows
+
     def start(self):
+        """Starts nvidia-smi (50 ms period) and returns once it has written its first
+        sample (at most 3 s), so that a short timed region that begins right after
+        still falls inside the sampling."""
         fd, self.path = tempfile.mkstemp(suffix=".csv")
         os.close(fd)
+        self.n0 = 0
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", self.gpu, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+                 "-lms", "50"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
+            return
+        t0 = time.time()
+        while not self._rows() and time.time() - t0 < 3.0 and self.proc.poll() is None:
+            time.sleep(0.01)
+
+    def region_start(self):
+        """Marks the start of the timed region: samples written before it are dropped."""
+        if self.proc is not None:
+            self.n0 = len(self._rows())
 
     def stop(self):
         if self.proc is None:
@@ -96,12 +121,7 @@ class ClockSampler:
             self.proc.wait(timeout=5)
         except Exception:
             self.proc.kill()
-        rows = []
-        with open(self.path) as f:
-            for line in f:
-                parts = [s.strip() for s in line.split(",")]
-                if len(parts) >= 9:
-                    rows.append(parts)
+        rows = self._rows()[self.n0:]
         os.unlink(self.path)
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
@@ -336,6 +356,7 @@ def run_ours(args):
         torch.cuda.synchronize(dev)
         clocks.start()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        clocks.region_start()
         e0.record(stream)
         for _ in range(args.steps):
             y, _ = mod(x, attn_mask=mask)
@@ -581,6 +602,7 @@ def run_seq_sharded(args):
         torch.cuda.synchronize(dev)
         clocks.start()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        clocks.region_start()
         e0.record(stream)
         for _ in range(args.steps):
             y = seqshard.sequence_sharded_forward(mod, xs, layout=layout)
