@@ -88,7 +88,9 @@ struct LtLayout {
   static constexpr int offU = offStage + 2 * kStage;   // U partial sums [CQ][3][128]
   static constexpr int offMisc = offU + CQ * 3 * 128 * 4;
   static constexpr int offBar = offMisc + 64;
-  static constexpr int kBytes = offBar + 128;
+  // banked layout: the slot of every (column v, lane u) of a diagonal block, uint16 [32][32]
+  static constexpr int offDiag = offBar + 128;
+  static constexpr int kBytes = offDiag + 32 * 32 * 2;
   static_assert(NCH <= 4, "one operand barrier per column chunk, at most 4");
   // TMEM: R^T hi, R^T lo, A, P, Q (DP columns each), rounded up to a power of two.
   static constexpr uint32_t kTmemCols = 5 * DP <= 128 ? 128 : (5 * DP <= 256 ? 256 : 512);
@@ -288,6 +290,7 @@ __global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, LtLayout<DP>::kMinBloc
   int* s_nsq = smax + 8;                                           // squarings of this position
   volatile int* s_abort = smax + 9;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::offBar);
+  uint16_t* dtab = reinterpret_cast<uint16_t*>(sm + L::offDiag);
   // operands ready (compute -> MMA), one barrier per column chunk j: P1 has its
   // own set (its hand-over follows P4's without a wait in between); P2, P3,
   // squarings and P4 share the other
@@ -313,6 +316,12 @@ __global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, LtLayout<DP>::kMinBloc
     *s_nsq = 0;
     *s_abort = 0;
     fence_mbar_init();
+  }
+  if constexpr (BANKED) {
+    for (int i = threadIdx.x; i < 32 * 32; i += blockDim.x) {
+      const int v = i >> 5, u = i & 31;
+      dtab[i] = (uint16_t)(u == v ? 0 : gen_banked_diag(u, v));
+    }
   }
   if (warp == 0) {
     tmem_alloc(tmem_slot, L::kTmemCols);
@@ -452,46 +461,65 @@ __global__ void __launch_bounds__(LtLayout<DP>::NTHREADS, LtLayout<DP>::kMinBloc
       } else if (g < bc) {                         // upper rows: this lane's line, 16-byte loads
         const int bp = g * NB - g * (g + 1) / 2 + (bc - g - 1);
         const int line = (bp * 32 + lid) * 32, sw = lid & 7;
+        auto slot = [&](int j, int k) { return line + 4 * ((((cv + 8 * j) >> 2) + (k >> 2)) ^ sw) + (k & 3); };
 #pragma unroll
-        for (int j = 0; j < NCH; ++j) {
+        for (int j = 0; j < NCH; ++j)
 #pragma unroll
           for (int h2 = 0; h2 < 2; ++h2) {
-            const int pos = 4 * ((((cv + 8 * j) >> 2) + h2) ^ sw);
-            const float4 x = *reinterpret_cast<const float4*>(av + line + pos);
-            float xv[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              if (bias_h != nullptr) xv[e] += __ldg(bias_h + line + pos + e);
-              ev[j][4 * h2 + e] = __fmul_rn(xv[e], es);
-            }
+            const float4 x = *reinterpret_cast<const float4*>(av + slot(j, 4 * h2));
+            ev[j][4 * h2] = x.x; ev[j][4 * h2 + 1] = x.y; ev[j][4 * h2 + 2] = x.z; ev[j][4 * h2 + 3] = x.w;
           }
+        if (bias_h != nullptr) {
+#pragma unroll
+          for (int j = 0; j < NCH; ++j)
+#pragma unroll
+            for (int k = 0; k < 8; ++k) ev[j][k] += __ldg(bias_h + slot(j, k));
         }
+#pragma unroll
+        for (int j = 0; j < NCH; ++j)
+#pragma unroll
+          for (int k = 0; k < 8; ++k) ev[j][k] = __fmul_rn(ev[j][k], es);
       } else if (g > bc) {                         // lower rows: one line per column
         const int bp = bc * NB - bc * (bc + 1) / 2 + (g - bc - 1);
         const int line0 = (bp * 32 + cv) * 32;
+        // (cv + 8j + i) mod 8 = i
+        auto slot = [&](int j, int i) { return line0 + (8 * j + i) * 32 + (lid ^ (4 * i)); };
 #pragma unroll
         for (int j = 0; j < NCH; ++j)
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const int slot = line0 + (8 * j + i) * 32 + (lid ^ (4 * i));   // (cv + 8j + i) mod 8 = i
-            float x = av[slot];
-            if (bias_h != nullptr) x += __ldg(bias_h + slot);
-            ev[j][i] = -__fmul_rn(x, es);
-          }
+          for (int i = 0; i < 8; ++i) ev[j][i] = av[slot(j, i)];
+        if (bias_h != nullptr) {
+#pragma unroll
+          for (int j = 0; j < NCH; ++j)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) ev[j][i] += __ldg(bias_h + slot(j, i));
+        }
+#pragma unroll
+        for (int j = 0; j < NCH; ++j)
+#pragma unroll
+          for (int i = 0; i < 8; ++i) ev[j][i] = -__fmul_rn(ev[j][i], es);
       } else {                                     // diagonal block
         const int base = ((NB * (NB - 1) / 2) * 32 + g * 16) * 32;
+        // branch-free: every lane loads, the lane with u = v from the block's first
+        // slot (in range; its value is discarded), so the warp's 32 loads stay one access;
+        // the slots come from the per-CTA table (gen_banked_diag, 0 for u = v)
+        auto slot = [&](int v) { return base + dtab[v * 32 + lid]; };
+#pragma unroll
+        for (int j = 0; j < NCH; ++j)
+#pragma unroll
+          for (int i = 0; i < 8; ++i) ev[j][i] = av[slot(cv + 8 * j + i)];
+        if (bias_h != nullptr) {
+#pragma unroll
+          for (int j = 0; j < NCH; ++j)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) ev[j][i] += __ldg(bias_h + slot(cv + 8 * j + i));
+        }
 #pragma unroll
         for (int j = 0; j < NCH; ++j)
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
-            // branch-free: every lane loads, the lane with u = v from the block's
-            // first slot (in range; its value is discarded), so the warp's 32
-            // loads stay one access
             const int v = cv + 8 * j + i;
-            const int slot = v == lid ? base : base + gen_banked_diag(lid, v);
-            float x = av[slot];
-            if (bias_h != nullptr) x += __ldg(bias_h + slot);
-            x = __fmul_rn(x, es);
+            const float x = __fmul_rn(ev[j][i], es);
             ev[j][i] = (v == lid) ? 0.f : ((v < lid) ? -x : x);
           }
       }
