@@ -98,6 +98,9 @@ HOA_DEVICE void warp_matvec(const float* __restrict__ Mat, const float* __restri
 // position; only R_t streams from HBM.
 constexpr int kXPos = 128;
 
+// DF: the head dim the R_t matvec is unrolled for (64, 96 or 120), or 0 for any d;
+// one instantiation per width keeps each at its own register count (occupancy).
+template <int DF>
 __global__ void __launch_bounds__(kXWarps * 32)
 out_transport_kernel(const float* __restrict__ o, const float* __restrict__ R,
                      const float* __restrict__ C, int chunk, int K, int nsub, void* out, int out_dtype,
@@ -140,8 +143,7 @@ out_transport_kernel(const float* __restrict__ o, const float* __restrict__ R,
       w[e] = acc;
     }
     __syncwarp();
-    if (d == 96) warp_matvec_fixed<96>(R + pos * d * d, w, xo, lane);
-    else if (d == 64) warp_matvec_fixed<64>(R + pos * d * d, w, xo, lane);
+    if constexpr (DF > 0) warp_matvec_fixed<DF>(R + pos * d * d, w, xo, lane);
     else warp_matvec(R + pos * d * d, w, xo, d, lane);
     const long long obase = (((long long)b * T + t) * H + h) * d;
     for (int e = lane; e < d; e += 32) store_elem(out, obase + e, out_dtype, xo[e]);
@@ -165,11 +167,11 @@ extern "C" int hoa_out_transport(const float* o, const float* R, const float* C,
   if (blocks > 0x7fffffffLL || d > 128) return HOA_ERR_UNSUPPORTED;
   const size_t smem = (size_t)(d * (d + 1) + kXWarps * 2 * d) * sizeof(float);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  auto* kern = d == 96 ? out_transport_kernel<96> : d == 64 ? out_transport_kernel<64>
+              : d == 120 ? out_transport_kernel<120> : out_transport_kernel<0>;
   if (smem > 48 * 1024 &&
-      cudaFuncSetAttribute(out_transport_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-          cudaSuccess)
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return HOA_ERR_LAUNCH;
-  out_transport_kernel<<<(unsigned)blocks, kXWarps * 32, smem, s>>>(
-      o, R, C, chunk, K, nsub, out, out_dtype, B * H, H, T, d);
+  kern<<<(unsigned)blocks, kXWarps * 32, smem, s>>>(o, R, C, chunk, K, nsub, out, out_dtype, B * H, H, T, d);
   return launch_status();
 }
