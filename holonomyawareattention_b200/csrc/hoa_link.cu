@@ -477,17 +477,25 @@ __global__ void __launch_bounds__(LinkRm<DP>::NT, 1) link_local_rm_kernel(LinkAr
     // compiler from holding all of them in registers across the position loop)
     int dl;
     asm volatile("mov.b32 %0, %1;" : "=r"(dl) : "r"(d));
+    // (packed layout only: the banked one needs d % 32 == 0, which no d of this kernel has;
+    // the element type is chosen outside the unrolled loops, so that no branch separates
+    // the loads and they are all in flight together)
     float gv[kPairsPerWarp][kPairChunks];
+    auto load_gen = [&](auto tag) {
+      using TA = decltype(tag);
+      const TA* ag = static_cast<const TA*>(p.a) + abase;
 #pragma unroll
-    for (int u = 0; u < kPairsPerWarp; ++u)
+      for (int u = 0; u < kPairsPerWarp; ++u)
 #pragma unroll
-      for (int c = 0; c < kPairChunks; ++c) {
-        int row, col;
-        const bool ok = pair_elem(warp + u * NW, lane + 32 * c, dl, row, col);
-        const int idx = row * (2 * dl - row - 1) / 2 + col - row - 1;
-        const int slot = p.a_banked ? gen_banked_slot(row, col, dl) : idx;
-        gv[u][c] = (ok && a_ok) ? load_elem(p.a, abase + slot, p.a_dtype) : 0.f;
-      }
+        for (int c = 0; c < kPairChunks; ++c) {
+          int row, col;
+          const bool ok = pair_elem(warp + u * NW, lane + 32 * c, dl, row, col) && a_ok;
+          const int idx = row * (2 * dl - row - 1) / 2 + col - row - 1;
+          gv[u][c] = ok ? static_cast<float>(ag[ok ? idx : 0]) : 0.f;
+        }
+    };
+    if (p.a_dtype == HOA_BF16) load_gen(__nv_bfloat16{});
+    else load_gen(float{});
     float qv[kVecPer];
 #pragma unroll
     for (int u = 0; u < kVecPer; ++u) {
@@ -506,6 +514,17 @@ __global__ void __launch_bounds__(LinkRm<DP>::NT, 1) link_local_rm_kernel(LinkAr
 #pragma unroll
     for (int u = 0; u < kVecPer; ++u)
       if (tid + u * NT < 3 * DP) svec[tid + u * NT] = qv[u];
+    if (p.a_bias != nullptr) {
+      const float* bh = p.a_bias + (long long)h * p.a_stride;
+#pragma unroll
+      for (int u = 0; u < kPairsPerWarp; ++u)
+#pragma unroll
+        for (int c = 0; c < kPairChunks; ++c) {
+          int row, col;
+          if (pair_elem(warp + u * NW, lane + 32 * c, dl, row, col))
+            gv[u][c] += bh[row * (2 * dl - row - 1) / 2 + col - row - 1];
+        }
+    }
     // ---- edge t: A = skew(edge_scale * a_t) ------------------------------
 #pragma unroll
     for (int u = 0; u < kPairsPerWarp; ++u)
@@ -513,12 +532,7 @@ __global__ void __launch_bounds__(LinkRm<DP>::NT, 1) link_local_rm_kernel(LinkAr
       for (int c = 0; c < kPairChunks; ++c) {
         int row, col;
         if (pair_elem(warp + u * NW, lane + 32 * c, dl, row, col)) {
-          float av = gv[u][c];
-          if (p.a_bias != nullptr) {
-            const int idx = row * (2 * dl - row - 1) / 2 + col - row - 1;
-            av += p.a_bias[(long long)h * p.a_stride + (p.a_banked ? gen_banked_slot(row, col, dl) : idx)];
-          }
-          const float v = __fmul_rn(av, p.edge_scale);
+          const float v = __fmul_rn(gv[u][c], p.edge_scale);
           bufA[row * DP + col] = v;
           bufA[col * DP + row] = -v;
         }
@@ -857,6 +871,7 @@ int launch_link_local(const LinkArgs& a, cudaStream_t s) {
   void (*kern)(LinkArgs);
   int nt;
   if constexpr (DP == 120) {
+    if (a.a_banked) return HOA_ERR_UNSUPPORTED;   // the banked layout needs d % 32 == 0
     kern = link_local_rm_kernel<DP>;
     nt = LinkRm<DP>::NT;
   } else {
