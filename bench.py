@@ -301,7 +301,7 @@ def generator_precision_label(mod, T, dtype):
     import torch
     if dtype == torch.float32:
         return "fp32"
-    eff = "split" if mod._split_generators(T) else "bf16"
+    eff = mod._generator_mode(T)
     return f"{eff} (auto)" if mod.generator_precision == "auto" else eff
 
 
@@ -587,6 +587,8 @@ def run_seq_sharded(args):
     with torch.device(dev):
         mod = PathOrderedGeometricMHA(D, n_heads=H, edge_scale=EDGE_SCALE)
     mod = mod.to(dtype).eval()
+    if args.generator_precision:
+        mod.generator_precision = args.generator_precision
     g = torch.Generator(device=dev).manual_seed(1000)
     x = torch.randn(B, T, D, device=dev, generator=g).to(dtype)       # same sequence on every rank
     layout = args.seq_layout
@@ -675,7 +677,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--config", default="c3", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--generator-precision", default=None, choices=[None, "auto", "split", "bf16"])
+    ap.add_argument("--generator-precision", default=None, choices=[None, "auto", "split", "split8", "bf16"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seq-layout", default="zigzag", choices=["zigzag", "contiguous"],
                     help="shard layout of the sequence-sharded configs")

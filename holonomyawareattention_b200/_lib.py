@@ -60,6 +60,10 @@ SIGNATURES = {
     "hoa_selftest_wait": (c_int, [c_void_p, ctypes.c_longlong, c_void_p]),
     "hoa_edge_gemm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p,
                               c_size_t, c_void_p]),
+    "hoa_edge_gelu_split8": (c_int, [c_void_p, c_void_p, c_void_p, ctypes.c_longlong, c_int, c_float,
+                                     c_void_p]),
+    "hoa_edge_gemm_fp8_acc": (c_int, [c_void_p, c_void_p, c_void_p, c_float, c_int, c_int, c_int, c_void_p,
+                                      c_size_t, c_void_p]),
 }
 
 _lock = threading.Lock()

@@ -60,8 +60,12 @@ class PathOrderedGeometricMHA(nn.Module):
         its high and low bf16 halves ([h_hi | h_lo] against [W2^T ; W2^T], fp32
         output), so the generators carry ~16 bits (3.7e-3 at both lengths) at
         twice the GEMM cost;
-      * "auto" (default): "bf16" for sequences of up to 8192 positions, "split"
-        beyond.
+      * "split8": the high half as in "split", the low half (at most 2^-9 of
+        the high one) in e4m3 against W2 in e4m3 in an fp8 GEMM that adds into
+        the bf16 GEMM's fp32 output: ~13-bit generators at 1.5 times the
+        bf16 GEMM's cost;
+      * "auto" (default): "bf16" for sequences of up to 8192 positions, "split8"
+        beyond ("split" where the fp8 GEMM does not take the shapes).
     In float32 the edge MLP runs in fp32, exactly as the reference.
     """
 
@@ -194,11 +198,25 @@ class PathOrderedGeometricMHA(nn.Module):
             return F.linear(self.edge_mlp[1](lin0(pair)), w2, b2), None, layout
         if x.dtype != torch.bfloat16:
             raise NotImplementedError(f"dtype {x.dtype} is not supported (float32 or bfloat16)")
-        split = self._split_generators(seq_len if seq_len is not None else
-                                       (L if x_next is None else None))
+        mode = self._generator_mode(seq_len if seq_len is not None else
+                                    (L if x_next is None else None))
         p2 = pair.reshape(B * L, 2 * D)
         w1t, b1 = self._w1t()
         h = ops.edge_gemm(p2, w1t, b1)            # fp32 out, the bias added in the epilogue
+        if mode == "split8" and not self._fp8_shape_ok(B * L, h.shape[1]):
+            mode = "split"                        # shapes the fp8 GEMM does not take
+        if mode == "split8":
+            # W2 g_hi in bf16 (the bias in the epilogue), then += W2 g_lo with both operands in
+            # e4m3 (hoa_edge_gelu_split8, hoa_edge_gemm_fp8_acc)
+            hi, lo = ops.edge_gelu_split8(h)
+            del h
+            wt, bias = self._stacked_w2t(False)
+            a = ops.edge_gemm(hi, wt, bias)
+            del hi
+            w8, alpha = self._w2_fp8()
+            ops.edge_gemm_fp8_acc(lo, w8, a, alpha)
+            return a.view(B, L, -1), None, layout
+        split = mode != "bf16"
         # GEMM operand [g_hi | g_lo] ("bf16": g_hi), g = GELU(h), in one pass (hoa_edge_gelu_split),
         # against [W2^T ; W2^T] (W2^T): W2 g_hi + W2 g_lo in fp32, the bias added in the GEMM's
         # epilogue (hoa_edge_gemm, cuBLASLt)
@@ -211,15 +229,44 @@ class PathOrderedGeometricMHA(nn.Module):
     # sequences longer than this use the split generators under "auto"
     AUTO_SPLIT_ABOVE = 8192
 
-    def _split_generators(self, L: Optional[int]) -> bool:
-        """Whether the bf16 edge MLP runs split for a sequence of L positions
-        (None: a shard of a longer sequence, always split under "auto")."""
+    def _generator_mode(self, L: Optional[int]) -> str:
+        """The bf16 edge MLP's form for a sequence of L positions: "bf16", "split" or "split8"
+        (None: a shard of a longer sequence, always a split form under "auto")."""
         p = self.generator_precision
-        if p not in ("auto", "split", "bf16"):
-            raise ValueError("generator_precision must be 'auto', 'split' or 'bf16'")
+        if p not in ("auto", "split", "split8", "bf16"):
+            raise ValueError("generator_precision must be 'auto', 'split', 'split8' or 'bf16'")
         if p == "auto":
-            return L is None or L > self.AUTO_SPLIT_ABOVE
-        return p == "split"
+            return self.AUTO_LONG if (L is None or L > self.AUTO_SPLIT_ABOVE) else "bf16"
+        return p
+
+    # the split form "auto" uses beyond AUTO_SPLIT_ABOVE (same accuracy as "split", measured
+    # at T = 65536, with the low half's GEMM in fp8)
+    AUTO_LONG = "split8"
+
+    def _fp8_shape_ok(self, M: int, K: int) -> bool:
+        """Whether the fp8 GEMM of "split8" takes M rows x K hidden x the generator width
+        (multiples of 16); otherwise "split" runs."""
+        N = self.h * ops.gen_stride(self.d, self._gen_layout())
+        return M % 16 == 0 and K % 16 == 0 and N % 16 == 0
+
+    def _split_generators(self, L: Optional[int]) -> bool:
+        """Whether the bf16 edge MLP runs a split form (the hidden layer's low half kept) for a
+        sequence of L positions (None: a shard of a longer sequence)."""
+        return self._generator_mode(L) != "bf16"
+
+    def _w2_fp8(self):
+        """(W2 in e4m3 (rows in the generator layout) times a power-of-two scale s, and
+        alpha = 1 / (s * ops.SPLIT8_LO_SCALE)), cached until edge_mlp.2 changes."""
+        w = self.edge_mlp[2].weight
+        key = (w.data_ptr(), w._version, w.dtype, str(w.device))
+        if getattr(self, "_w2fp8_key", None) != key:
+            wr, _ = self._w2_rows(w.detach(), self.edge_mlp[2].bias.detach())
+            wf = wr.float()
+            amax = float(wf.abs().max())
+            s = 2.0 ** math.floor(math.log2(448.0 / amax)) if amax > 0 else 1.0
+            self._w2fp8 = ((wf * s).to(torch.float8_e4m3fn).contiguous(), 1.0 / (s * ops.SPLIT8_LO_SCALE))
+            self._w2fp8_key = key
+        return self._w2fp8
 
     def _stacked_w2t(self, split: bool = True):
         """([W2^T ; W2^T] (8D x m*H; W2^T alone for split=False) in bf16, the output bias in

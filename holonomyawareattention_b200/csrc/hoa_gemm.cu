@@ -7,6 +7,7 @@
 // B_cm = hidden (row-major M x K) viewed as K x M (leading dimension K); the
 // bias runs along D_cm's rows (length N).
 #include <cublasLt.h>
+#include <cuda_fp8.h>
 
 #include <map>
 #include <mutex>
@@ -25,7 +26,8 @@ struct GemmPlan {
 
 std::mutex g_mu;
 cublasLtHandle_t g_handle = nullptr;
-using PlanKey = std::tuple<int, int, int, bool, size_t>;  // M, N, K, bias, workspace bytes
+using PlanKey = std::tuple<int, int, int, int, size_t>;  // M, N, K, kind (0 / 1: bf16 without / with
+                                                         // bias, 2: fp8 accumulate), workspace bytes
 std::map<PlanKey, GemmPlan> g_plans;
 
 void destroy_plan(GemmPlan& p) {
@@ -81,7 +83,7 @@ extern "C" int hoa_edge_gemm(const void* hidden, const void* wt, const float* bi
   // descriptor and the enqueue of the matmul that reads it
   std::lock_guard<std::mutex> lock(g_mu);
   if (g_handle == nullptr && cublasLtCreate(&g_handle) != CUBLAS_STATUS_SUCCESS) return HOA_ERR_LAUNCH;
-  const PlanKey key{M, N, K, bias != nullptr, workspace_bytes};
+  const PlanKey key{M, N, K, bias != nullptr ? 1 : 0, workspace_bytes};
   auto it = g_plans.find(key);
   if (it == g_plans.end()) {
     GemmPlan p;
@@ -98,6 +100,63 @@ extern "C" int hoa_edge_gemm(const void* hidden, const void* wt, const float* bi
   const float one = 1.f, zero = 0.f;
   const cublasStatus_t st =
       cublasLtMatmul(g_handle, plan.op, &one, wt, plan.a, hidden, plan.b, &zero, out, plan.d, out, plan.d,
+                     &plan.algo, workspace, plan.ws, reinterpret_cast<cudaStream_t>(stream));
+  return st == CUBLAS_STATUS_SUCCESS ? HOA_OK : HOA_ERR_LAUNCH;
+}
+
+// hoa_edge_gemm_fp8_acc: out (M x N, fp32, row-major) += alpha * lo (M x K, e4m3) W^T, with
+// W (N x K, e4m3) the output projection's weight as stored (rows = outputs).  Both operands
+// are K-major, cuBLASLt's FP8 form: D_cm (N x M) = op(A) B with A = W viewed as K x N
+// (transposed) and B = lo viewed as K x M; C = D = out (beta = 1).
+namespace {
+int make_plan_fp8(GemmPlan& p, int M, int N, int K, size_t ws_bytes) {
+  if (cublasLtMatmulDescCreate(&p.op, CUBLAS_COMPUTE_32F, CUDA_R_32F) != CUBLAS_STATUS_SUCCESS)
+    return HOA_ERR_LAUNCH;
+  const cublasOperation_t ta = CUBLAS_OP_T, tb = CUBLAS_OP_N;
+  cublasLtMatmulDescSetAttribute(p.op, CUBLASLT_MATMUL_DESC_TRANSA, &ta, sizeof(ta));
+  cublasLtMatmulDescSetAttribute(p.op, CUBLASLT_MATMUL_DESC_TRANSB, &tb, sizeof(tb));
+  if (cublasLtMatrixLayoutCreate(&p.a, CUDA_R_8F_E4M3, K, N, K) != CUBLAS_STATUS_SUCCESS ||
+      cublasLtMatrixLayoutCreate(&p.b, CUDA_R_8F_E4M3, K, M, K) != CUBLAS_STATUS_SUCCESS ||
+      cublasLtMatrixLayoutCreate(&p.d, CUDA_R_32F, N, M, N) != CUBLAS_STATUS_SUCCESS)
+    return HOA_ERR_LAUNCH;
+  cublasLtMatmulPreference_t pref = nullptr;
+  if (cublasLtMatmulPreferenceCreate(&pref) != CUBLAS_STATUS_SUCCESS) return HOA_ERR_LAUNCH;
+  cublasLtMatmulPreferenceSetAttribute(pref, CUBLASLT_MATMUL_PREF_MAX_WORKSPACE_BYTES, &ws_bytes,
+                                       sizeof(ws_bytes));
+  cublasLtMatmulHeuristicResult_t res[1];
+  int found = 0;
+  const cublasStatus_t st =
+      cublasLtMatmulAlgoGetHeuristic(g_handle, p.op, p.a, p.b, p.d, p.d, pref, 1, res, &found);
+  cublasLtMatmulPreferenceDestroy(pref);
+  if (st != CUBLAS_STATUS_SUCCESS || found < 1) return HOA_ERR_UNSUPPORTED;
+  p.algo = res[0].algo;
+  p.ws = res[0].workspaceSize;
+  return HOA_OK;
+}
+}  // namespace
+
+extern "C" int hoa_edge_gemm_fp8_acc(const void* lo, const void* w, float* out, float alpha, int M, int N,
+                                     int K, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!lo || !w || !out || M < 1 || N < 1 || K < 1 || (workspace_bytes > 0 && !workspace))
+    return HOA_ERR_INVALID_ARG;
+  if ((K & 15) != 0 || (N & 15) != 0 || (M & 15) != 0) return HOA_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(g_mu);
+  if (g_handle == nullptr && cublasLtCreate(&g_handle) != CUBLAS_STATUS_SUCCESS) return HOA_ERR_LAUNCH;
+  const PlanKey key{M, N, K, 2, workspace_bytes};
+  auto it = g_plans.find(key);
+  if (it == g_plans.end()) {
+    GemmPlan p;
+    const int st = make_plan_fp8(p, M, N, K, workspace_bytes);
+    if (st != HOA_OK) {
+      destroy_plan(p);
+      return st;
+    }
+    it = g_plans.emplace(key, p).first;
+  }
+  const GemmPlan& plan = it->second;
+  const float one = 1.f;
+  const cublasStatus_t st =
+      cublasLtMatmul(g_handle, plan.op, &alpha, w, plan.a, lo, plan.b, &one, out, plan.d, out, plan.d,
                      &plan.algo, workspace, plan.ws, reinterpret_cast<cudaStream_t>(stream));
   return st == CUBLAS_STATUS_SUCCESS ? HOA_OK : HOA_ERR_LAUNCH;
 }
@@ -150,5 +209,53 @@ extern "C" int hoa_edge_gelu_split(const float* h, void* out, long long rows, in
   if (blocks > 148LL * 64) blocks = 148LL * 64;
   edge_gelu_split_kernel<<<(unsigned)blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       h, static_cast<__nv_bfloat16*>(out), rows, cols, split ? 1 : 0);
+  return cudaGetLastError() == cudaSuccess ? HOA_OK : HOA_ERR_LAUNCH;
+}
+
+// The same hidden layer for the fp8 form: g_hi = bf16(g) (rows x cols, bf16) and the remainder
+// g - g_hi, which is at most 2^-9 |g|, times lo_scale (a power of two) in e4m3 with saturation
+// (rows x cols, one byte each), the operand of hoa_edge_gemm_fp8_acc.
+namespace {
+
+__global__ void edge_gelu_split8_kernel(const float* __restrict__ h, __nv_bfloat16* __restrict__ hi,
+                                        uint8_t* __restrict__ lo, long long rows, int cols, float lo_scale) {
+  const int c4 = cols >> 2;
+  const long long n4 = rows * c4;
+  const float kAlpha = 0.70710678118654752440f;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / c4;
+    const int c = (int)(i % c4) * 4;
+    const float4 x = *reinterpret_cast<const float4*>(h + r * cols + c);
+    const float xv[4] = {x.x, x.y, x.z, x.w};
+    uint32_t hw[4], lw = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float g = xv[k] * 0.5f * (1.0f + erff(xv[k] * kAlpha));
+      const __nv_bfloat16 hb = __float2bfloat16_rn(g);
+      hw[k] = __bfloat16_as_ushort(hb);
+      const __nv_fp8_storage_t l8 =
+          __nv_cvt_float_to_fp8((g - __bfloat162float(hb)) * lo_scale, __NV_SATFINITE, __NV_E4M3);
+      lw |= (uint32_t)l8 << (8 * k);
+    }
+    *reinterpret_cast<uint2*>(hi + r * cols + c) = make_uint2(hw[0] | (hw[1] << 16), hw[2] | (hw[3] << 16));
+    *reinterpret_cast<uint32_t*>(lo + r * cols + c) = lw;
+  }
+}
+
+}  // namespace
+
+extern "C" int hoa_edge_gelu_split8(const float* h, void* hi, void* lo, long long rows, int cols,
+                                    float lo_scale, void* stream) {
+  if (!h || !hi || !lo || rows < 1 || cols < 4 || (cols & 3) != 0 || !(lo_scale > 0.f))
+    return HOA_ERR_INVALID_ARG;
+  if ((reinterpret_cast<uintptr_t>(h) & 15) != 0 || (reinterpret_cast<uintptr_t>(hi) & 7) != 0 ||
+      (reinterpret_cast<uintptr_t>(lo) & 3) != 0)
+    return HOA_ERR_INVALID_ARG;
+  const long long n4 = rows * (cols >> 2);
+  long long blocks = (n4 + 255) / 256;
+  if (blocks > 148LL * 64) blocks = 148LL * 64;
+  edge_gelu_split8_kernel<<<(unsigned)blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      h, static_cast<__nv_bfloat16*>(hi), static_cast<uint8_t*>(lo), rows, cols, lo_scale);
   return cudaGetLastError() == cudaSuccess ? HOA_OK : HOA_ERR_LAUNCH;
 }

@@ -513,8 +513,52 @@ def edge_gelu_split(h: torch.Tensor, split: bool) -> torch.Tensor:
     return out
 
 
+# fixed scale of the fp8 low half: g - bf16(g) is at most 2^-9 |g|, so 2^12 maps |g| up to 56
+# onto e4m3's largest value (448, saturating beyond) and keeps remainders down to 2^-18 normal
+SPLIT8_LO_SCALE = 4096.0
+
+
+def edge_gelu_split8(h: torch.Tensor):
+    """GELU(h) (exact erf) of the fp32 hidden layer as (bf16(g), e4m3(SPLIT8_LO_SCALE * (g - bf16(g))))
+    (hoa_edge_gelu_split8), both (rows, cols)."""
+    _need_cuda(h)
+    if h.dtype != torch.float32 or h.dim() != 2 or not h.is_contiguous():
+        raise ValueError("h must be a contiguous 2-D fp32 tensor")
+    rows, cols = h.shape
+    hi = torch.empty(rows, cols, dtype=torch.bfloat16, device=h.device)
+    lo = torch.empty(rows, cols, dtype=torch.float8_e4m3fn, device=h.device)
+    _lib.call("hoa_edge_gelu_split8", _ptr(h), _ptr(hi), _ptr(lo), rows, cols, SPLIT8_LO_SCALE,
+              _stream(h.device))
+    return hi, lo
+
+
 _GEMM_WS = {}
 _GEMM_WS_BYTES = 32 << 20
+
+
+def _gemm_ws(dev):
+    ws = _GEMM_WS.get(dev)
+    if ws is None:
+        ws = _GEMM_WS[dev] = torch.empty(_GEMM_WS_BYTES, dtype=torch.uint8, device=dev)
+    return ws
+
+
+def edge_gemm_fp8_acc(lo: torch.Tensor, w: torch.Tensor, out: torch.Tensor, alpha: float) -> torch.Tensor:
+    """out (M,N) fp32 += alpha * lo (M,K) e4m3 @ w (N,K) e4m3 ^T (hoa_edge_gemm_fp8_acc), in place."""
+    _need_cuda(lo, w, out)
+    if lo.dtype != torch.float8_e4m3fn or w.dtype != torch.float8_e4m3fn or out.dtype != torch.float32:
+        raise ValueError("lo and w must be float8_e4m3fn, out float32")
+    lo = _contig(lo, "lo")
+    w = _contig(w, "w")
+    out = _contig(out, "out")
+    M, K = lo.shape
+    N = w.shape[0]
+    if w.shape[1] != K or out.shape != (M, N):
+        raise ValueError(f"shapes: lo {tuple(lo.shape)}, w {tuple(w.shape)}, out {tuple(out.shape)}")
+    dev = lo.device
+    _lib.call("hoa_edge_gemm_fp8_acc", _ptr(lo), _ptr(w), _ptr(out), float(alpha), M, N, K, _ptr(_gemm_ws(dev)),
+              _GEMM_WS_BYTES, _stream(dev))
+    return out
 
 
 def edge_gemm(hidden: torch.Tensor, wt: torch.Tensor, bias: Optional[torch.Tensor] = None) -> torch.Tensor:

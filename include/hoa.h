@@ -24,8 +24,8 @@
  *
  * Process-wide state (everything else keeps none, and may be called from
  * several host threads on different data):
- *   - hoa_edge_gemm keeps one cuBLASLt handle and a plan per GEMM shape, and
- *     serialises its calls with a lock;
+ *   - hoa_edge_gemm and hoa_edge_gemm_fp8_acc keep one cuBLASLt handle and a
+ *     plan per GEMM shape, and serialise their calls with a lock;
  *   - hoa_core_forward_noalloc computes in one static device array per GPU,
  *     shared by all its calls (see there), and caches that array's address
  *     per device;
@@ -318,6 +318,24 @@ int hoa_debug_bounds(int extent_shift, int* status);
  */
 int hoa_edge_gemm(const void* hidden, const void* wt, const float* bias, float* out, int M, int N,
                   int K, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * The low half of the edge MLP's second layer in fp8 (the same layer as hoa_edge_gemm,
+ * core/attention_fast_chunked.py:76; the reference computes it in one fp32 GEMM): with
+ * g = g_hi + g_lo, g_hi = bf16(g), the layer is W g_hi + W g_lo; the first term is a bf16
+ * hoa_edge_gemm and the second, whose terms are at most 2^-9 of the first's, this call:
+ *   hoa_edge_gelu_split8: g = GELU(h) (exact erf) for h (rows, cols) fp32 -> hi (rows, cols)
+ *     = bf16(g) and lo (rows, cols) = e4m3(lo_scale * (g - bf16(g))), saturating (one byte
+ *     each); cols % 4 == 0, h 16-byte aligned, lo_scale > 0 (a power of two keeps it exact);
+ *   hoa_edge_gemm_fp8_acc: out (M x N, fp32, row-major) += alpha * lo (M x K, e4m3,
+ *     row-major) * w^T, w (N x K, e4m3, row-major: the weight as nn.Linear stores it), fp32
+ *     accumulation; alpha undoes the two operands' scales.  M, N, K multiples of 16.
+ * The plan of each shape is made once and cached; calls are serialised inside the library.
+ */
+int hoa_edge_gelu_split8(const float* h, void* hi, void* lo, long long rows, int cols, float lo_scale,
+                         void* stream);
+int hoa_edge_gemm_fp8_acc(const void* lo, const void* w, float* out, float alpha, int M, int N, int K,
+                          void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * hoa_selftest_wait — no counterpart in the reference.  Diagnostic for the

@@ -223,3 +223,35 @@ def test_edge_gelu_split_matches_torch(rows, cols, split):
         assert torch.equal(out[:, cols:], (g - hi.float()).to(torch.bfloat16))
     else:
         assert out.shape == (rows, cols)
+
+
+@pytest.mark.parametrize("rows,cols", [(1, 4), (37, 96), (300, 6144)])
+def test_edge_gelu_split8_matches_torch(rows, cols):
+    """hoa_edge_gelu_split8: the high half is bf16(F.gelu(h)) bit for bit; the low half is
+    SPLIT8_LO_SCALE * (g - bf16(g)) rounded to e4m3 (within half an e4m3 step: 2^-4 relative,
+    or the subnormal spacing 2^-9 absolute)."""
+    torch.manual_seed(rows + cols)
+    h = 3 * torch.randn(rows, cols, device=DEV)
+    hi, lo = ops.edge_gelu_split8(h)
+    g = torch.nn.functional.gelu(h)
+    ref_hi = g.to(torch.bfloat16)
+    assert torch.equal(hi, ref_hi)
+    r = (g - ref_hi.float()) * ops.SPLIT8_LO_SCALE
+    assert float(r.abs().max()) <= 448.0                       # |h| <= 3 * 6: no saturation here
+    err = (lo.float() - r).abs()
+    assert bool((err <= r.abs() * 2.0 ** -4 + 2.0 ** -10).all())
+
+
+@pytest.mark.parametrize("M,N,K", [(64, 48, 32), (1024, 1152, 768)])
+def test_edge_gemm_fp8_acc_matches_torch(M, N, K):
+    """hoa_edge_gemm_fp8_acc adds alpha * lo @ w^T (e4m3 operands, fp32 accumulation) into out,
+    against an fp64 product of the same e4m3 values."""
+    torch.manual_seed(M + N + K)
+    lo = (4 * torch.randn(M, K, device=DEV)).to(torch.float8_e4m3fn)
+    w = (4 * torch.randn(N, K, device=DEV)).to(torch.float8_e4m3fn)
+    out0 = torch.randn(M, N, device=DEV)
+    out = out0.clone()
+    alpha = 2.0 ** -7
+    ops.edge_gemm_fp8_acc(lo, w, out, alpha)
+    ref = out0.double() + alpha * (lo.double() @ w.double().t())
+    assert rel_l2(out.cpu().numpy(), ref.cpu().numpy()) < 1e-6

@@ -77,6 +77,10 @@ def test_generator_precision_policy():
     assert m._split_generators(128)
     m.generator_precision = "bf16"
     assert not m._split_generators(65536)
+    m.generator_precision = "split8"
+    assert m._split_generators(128) and m._generator_mode(128) == "split8"
+    m.generator_precision = "auto"
+    assert m._generator_mode(4096) == "bf16" and m._generator_mode(None) == m.AUTO_LONG
     m.generator_precision = "fp8"
     with pytest.raises(ValueError):
         m._split_generators(128)

@@ -205,10 +205,10 @@ def test_config2_full_size(dtype):
     assert O.rel_l2(y, ref) <= (FP32_TOL if dtype == torch.float32 else BF16_TOL)
 
 
-@pytest.mark.parametrize("precision", ["auto", "split"])
+@pytest.mark.parametrize("precision", ["auto", "split", "split8"])
 def test_config3_slice_bf16(precision):
     """configs[2] shape (T=4096, d_model=1536, H=16, bf16) on two batch rows vs fp32 torch
-    restatement, with the default generator precision (bf16 at this length) and the split one."""
+    restatement, with the default generator precision (bf16 at this length) and the split ones."""
     B, T, D, H, es = 2, 4096, 1536, 16, 0.05
     sd, x = seeded_case(D, H, seed=0, B=B, L=T, bf16_round=True)
     m = PathOrderedGeometricMHA(D, n_heads=H, edge_scale=es)
@@ -218,7 +218,7 @@ def test_config3_slice_bf16(precision):
     y = run(m, x.to(DEV, torch.bfloat16))
     ref = torch_ref.module_forward(sd, x.to(DEV), H, es, torch.float32, batch_slice=1).cpu().numpy()
     err = O.rel_l2(y, ref)
-    print(f"c3 slice bf16 rel-L2 {err:.3e}")
+    print(f"c3 slice bf16 ({precision}) rel-L2 {err:.3e}")
     assert err <= BF16_TOL
 
 
@@ -247,16 +247,18 @@ def test_config3_full_batch_bf16():
     assert err <= BF16_TOL and err_q <= BF16_TOL
 
 
-def test_config5_long_sequence_bf16():
+@pytest.mark.parametrize("precision", ["auto", "split"])
+def test_config5_long_sequence_bf16(precision):
     """one sequence of T = 65536 (d_model 1536, H 16, head_dim 96, bf16) on one GPU
     against the fp32 torch restatement (core/attention_fast_chunked.py:89-94: the sequential
     product over 65535 edges, the drift stress of this config), run two heads at a time to
-    bound its memory.  "auto" selects the split generators at this length."""
+    bound its memory.  "auto" selects a split form of the generators at this length."""
     B, T, D, H, es = 1, 65536, 1536, 16, 0.05
     sd, x = seeded_case(D, H, seed=0, B=B, L=T, bf16_round=True)
     m = PathOrderedGeometricMHA(D, n_heads=H, edge_scale=es)
     m.load_state_dict(sd)
     m = m.to(DEV, torch.bfloat16).eval()
+    m.generator_precision = precision
     assert m._split_generators(T)
     y = run(m, x.to(DEV, torch.bfloat16))
     del m
@@ -264,7 +266,7 @@ def test_config5_long_sequence_bf16():
     ref = torch_ref.module_forward(sd, x.to(DEV), H, es, torch.float32, batch_slice=1,
                                    head_group=2).cpu().numpy()
     err, err_q = rel_l2_whole_and_last_quarter(y, ref)
-    print(f"configs[4] T=65536 bf16: rel-L2 {err:.3e}, last quarter {err_q:.3e}")
+    print(f"configs[4] T=65536 bf16 ({precision}): rel-L2 {err:.3e}, last quarter {err_q:.3e}")
     assert err <= BF16_TOL and err_q <= BF16_TOL
 
 
