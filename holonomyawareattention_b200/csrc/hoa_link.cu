@@ -352,6 +352,16 @@ template <int DP> struct LinkRm {
   static_assert(DP % 8 == 0 && DP % RI == 0 && HALF == 4 * GC, "two runs of 4 GC columns");
 };
 
+// (a0, a1) = fma((x, x), (y0, y1), (a0, a1)): one packed fp32 FMA instruction, each lane
+// rounded as fmaf rounds it (sm_100 fma.rn.f32x2), half the instructions of two fmaf.
+HOA_DEVICE void fma2(float& a0, float& a1, unsigned long long xx, float y0, float y1) {
+  unsigned long long a, y;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(a) : "f"(a0), "f"(a1));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(y) : "f"(y0), "f"(y1));
+  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(a) : "l"(xx), "l"(y));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a0), "=f"(a1) : "l"(a));
+}
+
 template <int DP>
 HOA_DEVICE void mm_rm(const float* __restrict__ X, const float* __restrict__ Y, int ty, int tx,
                       float (&acc)[LinkRm<DP>::RI][8]) {
@@ -370,14 +380,12 @@ HOA_DEVICE void mm_rm(const float* __restrict__ X, const float* __restrict__ Y, 
 #pragma unroll
       for (int i = 0; i < RI; ++i) {
         const float x = kk == 0 ? xv[i].x : (kk == 1 ? xv[i].y : (kk == 2 ? xv[i].z : xv[i].w));
-        acc[i][0] = fmaf(x, y0.x, acc[i][0]);
-        acc[i][1] = fmaf(x, y0.y, acc[i][1]);
-        acc[i][2] = fmaf(x, y0.z, acc[i][2]);
-        acc[i][3] = fmaf(x, y0.w, acc[i][3]);
-        acc[i][4] = fmaf(x, y1.x, acc[i][4]);
-        acc[i][5] = fmaf(x, y1.y, acc[i][5]);
-        acc[i][6] = fmaf(x, y1.z, acc[i][6]);
-        acc[i][7] = fmaf(x, y1.w, acc[i][7]);
+        unsigned long long xx;
+        asm("mov.b64 %0, {%1, %1};" : "=l"(xx) : "f"(x));
+        fma2(acc[i][0], acc[i][1], xx, y0.x, y0.y);
+        fma2(acc[i][2], acc[i][3], xx, y0.z, y0.w);
+        fma2(acc[i][4], acc[i][5], xx, y1.x, y1.y);
+        fma2(acc[i][6], acc[i][7], xx, y1.z, y1.w);
       }
     }
   }
