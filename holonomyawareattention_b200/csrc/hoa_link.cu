@@ -828,10 +828,20 @@ carry_apply_kernel(const float* __restrict__ U, const float* __restrict__ Cin, v
         for (int i = 0; i < TR; ++i) xa[i] = Ut[r * kApplyLd + row0 + i];
 #pragma unroll
         for (int j = 0; j < TN; ++j) yb[j] = Cs[r * DP + col0 + j];
+        if constexpr (TN % 2 == 0) {                    // packed pairs of columns (fma.rn.f32x2)
 #pragma unroll
-        for (int i = 0; i < TR; ++i)
+          for (int i = 0; i < TR; ++i) {
+            unsigned long long xx;
+            asm("mov.b64 %0, {%1, %1};" : "=l"(xx) : "f"(xa[i]));
 #pragma unroll
-          for (int j = 0; j < TN; ++j) acc[i][j] = fmaf(xa[i], yb[j], acc[i][j]);
+            for (int j = 0; j < TN; j += 2) fma2(acc[i][j], acc[i][j + 1], xx, yb[j], yb[j + 1]);
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < TR; ++i)
+#pragma unroll
+            for (int j = 0; j < TN; ++j) acc[i][j] = fmaf(xa[i], yb[j], acc[i][j]);
+        }
       }
 #pragma unroll
       for (int i = 0; i < TR; ++i) {
