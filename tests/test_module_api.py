@@ -84,3 +84,14 @@ def test_generator_precision_policy():
     m.generator_precision = "fp8"
     with pytest.raises(ValueError):
         m._split_generators(128)
+
+
+def test_split8_shape_rule():
+    """"split8" runs its fp8 GEMM only where rows, hidden width and generator width are
+    multiples of 16 (cuBLASLt's fp8 shapes); elsewhere the forward takes "split"."""
+    m = PathOrderedGeometricMHA(1536, n_heads=16)          # banked layout, 16 x 4608 generators
+    assert m._fp8_shape_ok(16384, 6144)
+    assert not m._fp8_shape_ok(16383, 6144)
+    assert not m._fp8_shape_ok(16384, 6140)
+    small = PathOrderedGeometricMHA(20, n_heads=4)          # d = 5: 4 x 10 packed generators
+    assert not small._fp8_shape_ok(16384, 80)
